@@ -1,0 +1,44 @@
+// Host-side internals shared by the native translation units.
+#pragma once
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "lz_api.h"
+#include "lz_types.h"
+#include "lz_driver.h"
+
+void lz_set_error(const char* fmt, ...);
+int lz_heap_device(LzHeap* h);
+int lz_heap_rank(LzHeap* h);
+int lz_heap_world(LzHeap* h);
+
+#define LZ_CUDA_TRY(call)                                                              \
+  do {                                                                                 \
+    cudaError_t e__ = (call);                                                          \
+    if (e__ != cudaSuccess) {                                                          \
+      lz_set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e__), __FILE__, \
+                   __LINE__);                                                          \
+      return LZE_CUDA;                                                                 \
+    }                                                                                  \
+  } while (0)
+
+// Communicator: device-visible state plus the heap layout.
+static constexpr size_t kLzFlagsBytes = 1 << 20;
+
+struct LzComm {
+  LzHeap* heap;           // nullptr for emulated ranks
+  size_t heap_bytes;
+  int device;
+  LzDevComm dev;          // copied by value into every launch
+  size_t oneshot_off;     // two stages of oneshot_bytes each (double buffered)
+  size_t oneshot_bytes;
+  size_t stage_off;       // general staging region
+  size_t stage_bytes;
+  size_t user_off;        // start of the user-allocatable region
+  int sm_count;
+  int* status_host;       // host view of dev.status
+};
+
+// Returns the heap offset of [p, p+bytes) when it lies in this rank's heap, or
+// (size_t)-1.
+size_t lz_comm_heap_offset(const LzComm* c, const void* p, size_t bytes);

@@ -1,0 +1,44 @@
+"""ctypes signatures of the native subsystems (declared when the symbol exists)."""
+from __future__ import annotations
+
+import ctypes as C
+
+c_size = C.c_size_t
+c_ptr = C.c_void_p
+c_int = C.c_int
+c_dbl = C.c_double
+c_u64 = C.c_uint64
+c_u32 = C.c_uint32
+P = C.POINTER
+
+_CUDA = {
+    # single-GPU emulation
+    "lz_emu_create": (c_int, c_int, c_size, c_size, c_size, c_dbl, P(c_ptr)),
+    "lz_emu_destroy": (c_int, c_ptr),
+    "lz_emu_heap_ptr": (c_ptr, c_ptr, c_int),
+    "lz_emu_user_offset": (c_size, c_ptr),
+    "lz_emu_status": (c_int, c_ptr, c_int),
+    "lz_emu_allreduce": (c_int, c_ptr, P(c_ptr), P(c_ptr), c_size, c_int, c_int, c_int, c_int, c_ptr),
+}
+
+_CPU = {}
+
+
+def declare(lib, sig) -> None:
+    for name, (res, *args) in _CUDA.items():
+        if hasattr(lib, name):
+            sig(lib, name, res, *args)
+
+
+def declare_cpu(lib, sig) -> None:
+    for name, (res, *args) in _CPU.items():
+        if hasattr(lib, name):
+            sig(lib, name, res, *args)
+
+
+def add_cuda(table: dict) -> None:
+    _CUDA.update(table)
+
+
+def add_cpu(table: dict) -> None:
+    _CPU.update(table)

@@ -1,0 +1,77 @@
+"""Single-GPU emulation of R ranks for testing the multi-rank kernels.
+
+The R "ranks" each own a heap allocated on the same GPU; a collective runs as
+ONE cooperative launch of grid (G, R) so that every block that waits on
+another is guaranteed to be co-resident. This exercises the exact kernel
+bodies (barriers, flags, partitioning, reduction order) used across GPUs,
+without NVLink and without NVLS (no multicast object with one device).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from .. import _native
+from ..utils.dtypes import lz_dtype
+from .comm import ALGOS, _CudaBuf
+
+MiB = 1 << 20
+
+
+class EmulatedWorld:
+    def __init__(self, world: int, heap_bytes: int = 256 * MiB, oneshot_bytes: int = 4 * MiB,
+                 stage_bytes: int = 64 * MiB, timeout_s: float = 5.0):
+        self.world = world
+        self._lib = _native.cuda()
+        self._emu = C.c_void_p()
+        _native.check(self._lib.lz_emu_create(world, heap_bytes, oneshot_bytes, stage_bytes,
+                                              timeout_s, C.byref(self._emu)), "lz_emu_create")
+        self.heap_bytes = heap_bytes
+        self._user_off = self._lib.lz_emu_user_offset(self._emu)
+        self._bump = self._user_off
+        self.device = torch.cuda.current_device()
+
+    def empty(self, shape, dtype) -> list[torch.Tensor]:
+        """Symmetric allocation: one tensor per emulated rank at the same offset."""
+        shape = tuple(shape) if isinstance(shape, (tuple, list)) else (int(shape),)
+        numel = 1
+        for s in shape:
+            numel *= s
+        nbytes = numel * torch.empty((), dtype=dtype).element_size()
+        off = (self._bump + 255) // 256 * 256
+        if off + nbytes > self.heap_bytes:
+            raise MemoryError("emulated heap exhausted")
+        self._bump = off + nbytes
+        out = []
+        for r in range(self.world):
+            base = self._lib.lz_emu_heap_ptr(self._emu, r)
+            buf = _CudaBuf(base + off, max(nbytes, 1), self)
+            t = torch.as_tensor(buf, device=f"cuda:{self.device}")[:nbytes]
+            out.append(t.view(dtype).view(shape))
+        return out
+
+    def allreduce(self, ins, outs, algo: str = "twoshot", nblocks: int = 0, nthreads: int = 0):
+        R = self.world
+        assert len(ins) == len(outs) == R
+        arr_in = (C.c_void_p * R)(*[t.data_ptr() for t in ins])
+        arr_out = (C.c_void_p * R)(*[t.data_ptr() for t in outs])
+        s = torch.cuda.current_stream()
+        rc = self._lib.lz_emu_allreduce(self._emu, arr_in, arr_out, ins[0].numel(),
+                                        lz_dtype(ins[0].dtype), ALGOS[algo], nblocks, nthreads,
+                                        s.cuda_stream)
+        _native.check(rc, f"emulated allreduce[{algo}]")
+
+    def status(self, r: int) -> int:
+        return self._lib.lz_emu_status(self._emu, r)
+
+    def close(self):
+        if self._emu:
+            self._lib.lz_emu_destroy(self._emu)
+            self._emu = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,86 @@
+"""Native allreduce across real GPUs (one process per GPU, NVLink peer memory and
+NVLS). Runs with every available GPU count among 2, 4, 8."""
+import pytest
+import torch
+
+from tests._mp import run_ranks
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _inputs(world, n, dtype, seed):
+    xs = []
+    for r in range(world):
+        g = torch.Generator(device="cuda").manual_seed(seed * 100 + r)
+        xs.append((torch.randn(n, device="cuda", generator=g) * 1e-2).to(dtype))
+    return xs
+
+
+def _worker(rank, world, cases):
+    import torch
+
+    from results_b200.config import Config
+    from results_b200.parallel.comm import Communicator
+
+    cfg = Config(user_bytes=256 << 20, stage_bytes=256 << 20, oneshot_bytes=4 << 20, timeout_s=10.0)
+    comm = Communicator(config=cfg)
+    out = []
+    for (algo, dtname, n, sym, exact) in cases:
+        dtype = getattr(torch, dtname)
+        if algo.startswith("nvls") and not comm.has_multicast:
+            out.append((algo, dtname, n, sym, "skipped-no-multicast"))
+            continue
+        xs = _inputs(world, n, dtype, seed=n % 9973)
+        ref_acc = xs[0].float().clone()
+        for x in xs[1:]:
+            ref_acc += x.float()
+        ref = ref_acc.to(dtype)
+        if sym:
+            comm.reset_alloc()
+            buf = comm.empty(n, dtype)
+            for _ in range(3):
+                buf.copy_(xs[rank])
+                comm.allreduce_(buf, algo=algo)
+            res = buf.clone()
+        else:
+            res = torch.empty_like(xs[rank])
+            for _ in range(3):
+                comm.allreduce_(xs[rank], res, algo=algo)
+        torch.cuda.synchronize()
+        comm.check()
+        if exact:
+            ok = torch.equal(res, ref)
+            err = (res.float() - ref.float()).abs().max().item()
+        else:
+            err = ((res.float() - ref_acc).abs().max() / ref_acc.abs().max().clamp_min(1e-30)).item()
+            ok = err < {torch.float32: 1e-5, torch.float16: 5e-3, torch.bfloat16: 2e-2}[dtype]
+        out.append((algo, dtname, n, sym, "ok" if ok else f"MISMATCH err={err}"))
+    comm.close()
+    return out
+
+
+CASES = [
+    ("oneshot", "bfloat16", 1000, False, True),
+    ("oneshot", "float32", 1 << 16, False, True),
+    ("twoshot", "bfloat16", (1 << 20) + 64, False, True),
+    ("twoshot", "float16", 1 << 20, False, True),
+    ("twoshot", "bfloat16", 1 << 21, True, True),
+    ("ring", "bfloat16", 1 << 20, False, False),
+    ("ring", "float32", (1 << 18) + 32, False, False),
+    ("rhd", "bfloat16", 1 << 20, False, False),
+    ("nvls", "bfloat16", 1 << 21, True, False),
+    ("nvls", "float32", 1 << 20, False, False),
+    ("nvls", "bfloat16", (1 << 20) + 64, False, False),
+    ("nvls_oneshot", "bfloat16", 1 << 14, False, False),
+]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_native_allreduce(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    cases = [c for c in CASES if not (c[0] == "rhd" and world & (world - 1))]
+    res = run_ranks(_worker, world, backend="nccl", args=(cases,), timeout=600,
+                    env={"NCCL_DEBUG": "WARN"})
+    bad = [r for rank_res in res for r in rank_res if r[-1] not in ("ok", "skipped-no-multicast")]
+    assert not bad, bad
