@@ -1,1 +1,385 @@
-// placeholder
+// CPU oracle of the LZC1 codec and of the fp8 packers. Bit-exact with the
+// GPU kernels (csrc/lz_codec.cu, csrc/lz_fp8.cu); used by the CPU test suite,
+// by the CPU/gloo compressed collectives and to validate GPU output.
+//
+// Reference counterparts: dietgpu's compress/decompress ops (a closed .so in
+// the reference, loaded at single_node_nccl_allreduce_benchmark/compressed_twoshot_allreduce.py:34-47)
+// and the fp8 pair packer of back_up/fp8_e4m3fn_pack_benchmark.cu:21-93.
+#include <stdint.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "../lz_codec_format.h"
+
+using namespace lzc;
+
+namespace {
+
+inline void split_elem(const uint8_t* data, int dt, uint32_t i, uint8_t* sym, uint8_t* raw) {
+  switch (dt) {
+    case DT_BF16: {
+      uint16_t u;
+      memcpy(&u, data + 2 * (size_t)i, 2);
+      *sym = sym_bf16(u);
+      raw[0] = raw_bf16(u);
+      break;
+    }
+    case DT_F16: {
+      uint16_t u;
+      memcpy(&u, data + 2 * (size_t)i, 2);
+      *sym = sym_f16(u);
+      raw[0] = raw_f16(u);
+      break;
+    }
+    case DT_F32: {
+      uint32_t u;
+      memcpy(&u, data + 4 * (size_t)i, 4);
+      *sym = sym_f32(u);
+      uint32_t r = raw_f32(u);
+      raw[0] = (uint8_t)r;
+      raw[1] = (uint8_t)(r >> 8);
+      raw[2] = (uint8_t)(r >> 16);
+      break;
+    }
+    default:
+      *sym = data[i];
+  }
+}
+
+inline void merge_elem(uint8_t* out, int dt, uint32_t i, uint8_t sym, const uint8_t* raw) {
+  switch (dt) {
+    case DT_BF16: {
+      uint16_t u = merge_bf16(sym, raw[0]);
+      memcpy(out + 2 * (size_t)i, &u, 2);
+      break;
+    }
+    case DT_F16: {
+      uint16_t u = merge_f16(sym, raw[0]);
+      memcpy(out + 2 * (size_t)i, &u, 2);
+      break;
+    }
+    case DT_F32: {
+      uint32_t r = raw[0] | ((uint32_t)raw[1] << 8) | ((uint32_t)raw[2] << 16);
+      uint32_t u = merge_f32(sym, r);
+      memcpy(out + 4 * (size_t)i, &u, 4);
+      break;
+    }
+    default:
+      out[i] = sym;
+  }
+}
+
+// Encodes one sub-block with the warp-interleaved rANS. Returns the stream
+// length in bytes before padding (states + words), or 0 on overflow of
+// `cap` bytes (cap = number of symbols of the sub-block).
+uint32_t encode_sub(const uint8_t* syms, uint32_t n, const EncSym* tab, uint8_t* out,
+                    uint32_t cap) {
+  uint32_t x[LANES];
+  for (int l = 0; l < LANES; ++l) x[l] = RANS_L;
+  std::vector<uint16_t> words;
+  words.reserve(n);
+  for (int j = SUB_STEPS - 1; j >= 0; --j) {
+    for (int l = 0; l < LANES; ++l) {
+      uint32_t i = (uint32_t)j * LANES + l;
+      if (i >= n) continue;
+      const EncSym& e = tab[syms[i]];
+      if (enc_needs_word(x[l], e.freq)) {
+        words.push_back((uint16_t)(x[l] & 0xFFFF));
+        x[l] >>= 16;
+      }
+    }
+    if (128u + 2u * (uint32_t)words.size() > cap) return 0;
+    for (int l = 0; l < LANES; ++l) {
+      uint32_t i = (uint32_t)j * LANES + l;
+      if (i >= n) continue;
+      x[l] = enc_update(x[l], tab[syms[i]]);
+    }
+  }
+  memcpy(out, x, 128);
+  if (!words.empty()) memcpy(out + 128, words.data(), 2 * words.size());
+  return 128u + 2u * (uint32_t)words.size();
+}
+
+// Decodes one sub-block; returns false on any inconsistency.
+bool decode_sub(const uint8_t* stream, uint32_t stream_bytes, const uint32_t* dec_tab, uint32_t n,
+                uint8_t* syms) {
+  if (stream_bytes < 128 || (stream_bytes - 128) % 2) return false;
+  uint32_t x[LANES];
+  memcpy(x, stream, 128);
+  const uint8_t* wbase = stream + 128;
+  int64_t E = (stream_bytes - 128) / 2;
+  for (int j = 0; j < SUB_STEPS; ++j) {
+    int need_lanes[LANES];
+    int k = 0;
+    for (int l = 0; l < LANES; ++l) {
+      uint32_t i = (uint32_t)j * LANES + l;
+      if (i >= n) continue;
+      uint32_t slot = x[l] & (PROB_SCALE - 1);
+      uint32_t ent = dec_tab[slot];
+      syms[i] = (uint8_t)(ent & 0xFF);
+      x[l] = dec_update(x[l], ent);
+      if (x[l] < RANS_L) need_lanes[k++] = l;
+    }
+    if (k > E) return false;
+    for (int q = 0; q < k; ++q) {
+      int64_t idx = E - k + q;
+      uint16_t w;
+      memcpy(&w, wbase + 2 * idx, 2);
+      x[need_lanes[q]] = (x[need_lanes[q]] << 16) | w;
+    }
+    E -= k;
+  }
+  if (E != 0) return false;
+  for (int l = 0; l < LANES; ++l)
+    if (x[l] != RANS_L) return false;
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+uint32_t lzc_tg_capacity(uint32_t n, int dt) { return tg_capacity_n(n, dt); }
+uint64_t lzc_max_stream_bytes(uint64_t n, int dt) { return max_stream_bytes(n, dt); }
+
+// Encodes one TG of n (<= TG_ELEMS) elements into `out` (capacity
+// tg_capacity_n). Returns the record size.
+int64_t lzc_tg_encode(const void* data, uint32_t n, int dt, void* out_) {
+  if (n > TG_ELEMS) return -1;
+  uint8_t* out = static_cast<uint8_t*>(out_);
+  const uint8_t* in = static_cast<const uint8_t*>(data);
+  const int rb = raw_bytes_per_elem(dt);
+  const uint32_t raw_bytes = pad16(n * (uint32_t)rb);
+  std::vector<uint8_t> syms(n);
+  uint8_t* raw = out + sizeof(TgHeader);
+  memset(raw, 0, raw_bytes);
+  uint32_t counts[256] = {0};
+  for (uint32_t i = 0; i < n; ++i) {
+    split_elem(in, dt, i, &syms[i], raw + (size_t)i * rb);
+    counts[syms[i]]++;
+  }
+  TgHeader h;
+  memset(&h, 0, sizeof(h));
+  h.magic = TG_MAGIC;
+  h.version = VERSION;
+  h.dtype = (uint8_t)dt;
+  h.n = n;
+  h.raw_bytes = raw_bytes;
+  uint8_t* symsec = raw + raw_bytes;
+  const uint32_t raw_sym_bytes = pad16(n);
+  bool use_ans = n > 0;
+  uint32_t ans_bytes = 0;
+  std::vector<uint8_t> ans;
+  if (use_ans) {
+    uint32_t freq[256];
+    normalize_freqs(counts, n, freq);
+    EncSym tab[256];
+    uint32_t cum = 0;
+    std::vector<uint32_t> table;
+    for (int s = 0; s < 256; ++s) {
+      tab[s] = make_enc_sym(freq[s] ? freq[s] : 1, cum);
+      if (freq[s]) table.push_back(((uint32_t)s << 16) | freq[s]);
+      cum += freq[s];
+    }
+    const uint32_t nsub = (n + SUB_ELEMS - 1) / SUB_ELEMS;
+    const uint32_t tab_bytes = pad16(4 * (uint32_t)table.size());
+    const uint32_t sizes_bytes = pad16(4 * nsub);
+    ans.assign(tab_bytes + sizes_bytes, 0);
+    memcpy(ans.data(), table.data(), 4 * table.size());
+    std::vector<uint32_t> sizes(nsub);
+    std::vector<uint8_t> sub(SUB_ELEMS + 16);
+    for (uint32_t b = 0; b < nsub && use_ans; ++b) {
+      const uint32_t sn = std::min(SUB_ELEMS, n - b * SUB_ELEMS);
+      memset(sub.data(), 0, sub.size());
+      uint32_t len = encode_sub(syms.data() + (size_t)b * SUB_ELEMS, sn, tab, sub.data(), sn);
+      if (len == 0) {
+        use_ans = false;
+        break;
+      }
+      sizes[b] = len;
+      ans.insert(ans.end(), sub.begin(), sub.begin() + pad16(len));
+    }
+    if (use_ans) {
+      memcpy(ans.data() + tab_bytes, sizes.data(), 4 * nsub);
+      ans_bytes = (uint32_t)ans.size();
+      if (ans_bytes >= raw_sym_bytes) use_ans = false;
+      h.nnz = (uint16_t)table.size();
+      h.nsub = (uint16_t)nsub;
+    }
+  }
+  if (use_ans) {
+    h.mode = MODE_ANS;
+    h.sym_bytes = ans_bytes;
+    memcpy(symsec, ans.data(), ans_bytes);
+  } else {
+    h.mode = MODE_RAW;
+    h.nnz = 0;
+    h.nsub = 0;
+    h.sym_bytes = raw_sym_bytes;
+    memset(symsec, 0, raw_sym_bytes);
+    memcpy(symsec, syms.data(), n);
+  }
+  h.total = (uint32_t)sizeof(TgHeader) + raw_bytes + h.sym_bytes;
+  memcpy(out, &h, sizeof(h));
+  return h.total;
+}
+
+// Decodes one TG record. Returns 0, or a negative code on a corrupt record.
+int lzc_tg_decode(const void* rec_, uint64_t rec_cap, void* out, uint32_t n, int dt) {
+  const uint8_t* rec = static_cast<const uint8_t*>(rec_);
+  if (rec_cap < sizeof(TgHeader)) return -2;
+  TgHeader h;
+  memcpy(&h, rec, sizeof(h));
+  if (h.magic != TG_MAGIC || h.version != VERSION || h.dtype != dt || h.n != n) return -3;
+  const int rb = raw_bytes_per_elem(dt);
+  if (h.raw_bytes != pad16(n * (uint32_t)rb) || h.total > rec_cap ||
+      h.total != sizeof(TgHeader) + h.raw_bytes + h.sym_bytes)
+    return -4;
+  const uint8_t* raw = rec + sizeof(TgHeader);
+  const uint8_t* symsec = raw + h.raw_bytes;
+  std::vector<uint8_t> syms(n);
+  if (h.mode == MODE_RAW) {
+    if (h.sym_bytes != pad16(n)) return -5;
+    memcpy(syms.data(), symsec, n);
+  } else if (h.mode == MODE_ANS) {
+    const uint32_t nsub = (n + SUB_ELEMS - 1) / SUB_ELEMS;
+    if (h.nsub != nsub || h.nnz == 0 || h.nnz > 256) return -6;
+    const uint32_t tab_bytes = pad16(4u * h.nnz), sizes_bytes = pad16(4 * nsub);
+    if (tab_bytes + sizes_bytes > h.sym_bytes) return -7;
+    uint32_t dec_tab[PROB_SCALE];
+    uint32_t cum = 0;
+    for (uint32_t k = 0; k < h.nnz; ++k) {
+      uint32_t e;
+      memcpy(&e, symsec + 4 * k, 4);
+      uint32_t s = e >> 16, f = e & 0xFFFF;
+      if (s > 255 || f == 0 || cum + f > PROB_SCALE) return -8;
+      for (uint32_t q = 0; q < f; ++q) dec_tab[cum + q] = dec_entry(s, f, q);
+      cum += f;
+    }
+    if (cum != PROB_SCALE) return -9;
+    const uint8_t* sizes_p = symsec + tab_bytes;
+    uint64_t off = tab_bytes + sizes_bytes;
+    for (uint32_t b = 0; b < nsub; ++b) {
+      uint32_t sz;
+      memcpy(&sz, sizes_p + 4 * b, 4);
+      if (off + pad16(sz) > h.sym_bytes) return -10;
+      const uint32_t sn = std::min(SUB_ELEMS, n - b * SUB_ELEMS);
+      if (!decode_sub(symsec + off, sz, dec_tab, sn, syms.data() + (size_t)b * SUB_ELEMS))
+        return -11;
+      off += pad16(sz);
+    }
+  } else {
+    return -12;
+  }
+  uint8_t* o = static_cast<uint8_t*>(out);
+  for (uint32_t i = 0; i < n; ++i) merge_elem(o, dt, i, syms[i], raw + (size_t)i * rb);
+  return 0;
+}
+
+// Whole-tensor compact stream. Returns bytes written or a negative code.
+int64_t lzc_encode(const void* data, uint64_t n, int dt, void* out_, uint64_t cap) {
+  if (cap < max_stream_bytes(n, dt)) return -1;
+  uint8_t* out = static_cast<uint8_t*>(out_);
+  const uint64_t ntg = num_tgs(n);
+  StreamHeader sh;
+  memset(&sh, 0, sizeof(sh));
+  sh.magic = STREAM_MAGIC;
+  sh.version = VERSION;
+  sh.dtype = (uint8_t)dt;
+  sh.tg_elems = TG_ELEMS;
+  sh.n_tg = (uint32_t)ntg;
+  sh.n_elems = n;
+  uint64_t off = sizeof(StreamHeader) + pad16_64(8 * ntg);
+  memset(out + sizeof(StreamHeader), 0, pad16_64(8 * ntg));
+  const int es = elem_bytes(dt);
+  for (uint64_t t = 0; t < ntg; ++t) {
+    const uint32_t tn = (uint32_t)std::min<uint64_t>(TG_ELEMS, n - t * TG_ELEMS);
+    memcpy(out + sizeof(StreamHeader) + 8 * t, &off, 8);
+    int64_t sz = lzc_tg_encode(static_cast<const uint8_t*>(data) + t * TG_ELEMS * es, tn, dt, out + off);
+    if (sz < 0) return sz;
+    off += (uint64_t)sz;
+  }
+  sh.total_bytes = off;
+  memcpy(out, &sh, sizeof(sh));
+  return (int64_t)off;
+}
+
+int lzc_decode(const void* stream_, uint64_t bytes, void* out, uint64_t n, int dt) {
+  const uint8_t* st = static_cast<const uint8_t*>(stream_);
+  if (bytes < sizeof(StreamHeader)) return -2;
+  StreamHeader sh;
+  memcpy(&sh, st, sizeof(sh));
+  if (sh.magic != STREAM_MAGIC || sh.version != VERSION || sh.dtype != dt || sh.n_elems != n ||
+      sh.tg_elems != TG_ELEMS || sh.n_tg != num_tgs(n) || sh.total_bytes > bytes)
+    return -3;
+  const int es = elem_bytes(dt);
+  for (uint64_t t = 0; t < sh.n_tg; ++t) {
+    uint64_t off;
+    memcpy(&off, st + sizeof(StreamHeader) + 8 * t, 8);
+    if (off >= sh.total_bytes) return -4;
+    const uint32_t tn = (uint32_t)std::min<uint64_t>(TG_ELEMS, n - t * TG_ELEMS);
+    int rc = lzc_tg_decode(st + off, sh.total_bytes - off, static_cast<uint8_t*>(out) + t * TG_ELEMS * es, tn, dt);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
+// Symbol histogram (for entropy reporting).
+void lzc_histogram(const void* data, uint64_t n, int dt, uint64_t* counts) {
+  uint8_t raw[4];
+  for (int s = 0; s < 256; ++s) counts[s] = 0;
+  for (uint64_t i = 0; i < n; ++i) {
+    uint8_t sym;
+    split_elem(static_cast<const uint8_t*>(data), dt, (uint32_t)i, &sym, raw);
+    counts[sym]++;
+  }
+}
+
+// ---- fp8 -------------------------------------------------------------------
+// e4m3 pair container (layout of back_up/fp8_e4m3fn_pack_benchmark.cu:21-31):
+// [15]=a.sign [14:11]=a.exp [10:7]=b.exp [6:4]=a.mant [3]=b.sign [2:0]=b.mant,
+// so bits 14..7 (the bf16 exponent byte) carry both exponents.
+void lz_cpu_pack_e4m3(const uint8_t* in, uint16_t* out, uint64_t npairs) {
+  for (uint64_t i = 0; i < npairs; ++i) {
+    const uint8_t a = in[2 * i], b = in[2 * i + 1];
+    out[i] = (uint16_t)(((a & 0x80u) << 8) | ((a & 0x78u) << 8) | ((b & 0x78u) << 4) |
+                        ((a & 0x07u) << 4) | ((b & 0x80u) >> 4) | (b & 0x07u));
+  }
+}
+
+void lz_cpu_unpack_e4m3(const uint16_t* in, uint8_t* out, uint64_t npairs) {
+  for (uint64_t i = 0; i < npairs; ++i) {
+    const uint16_t w = in[i];
+    out[2 * i] = (uint8_t)(((w >> 8) & 0x80u) | ((w >> 8) & 0x78u) | ((w >> 4) & 0x07u));
+    out[2 * i + 1] = (uint8_t)(((w << 4) & 0x80u) | ((w >> 4) & 0x78u) | (w & 0x07u));
+  }
+}
+
+// e5m2 pair container: two 5-bit exponents do not fit one byte, so the
+// container keeps the high 4 exponent bits of each value in bits 14..7 (the
+// symbol byte) and moves the remaining bits to the raw byte:
+// [15]=a.sign [14:11]=a.e[4:1] [10:7]=b.e[4:1] [6]=a.e[0] [5:4]=a.mant
+// [3]=b.sign [2]=b.e[0] [1:0]=b.mant
+void lz_cpu_pack_e5m2(const uint8_t* in, uint16_t* out, uint64_t npairs) {
+  for (uint64_t i = 0; i < npairs; ++i) {
+    const uint32_t a = in[2 * i], b = in[2 * i + 1];
+    const uint32_t ae = (a >> 2) & 0x1F, be = (b >> 2) & 0x1F;
+    out[i] = (uint16_t)(((a & 0x80u) << 8) | ((ae >> 1) << 11) | ((be >> 1) << 7) |
+                        ((ae & 1u) << 6) | ((a & 0x3u) << 4) | ((b & 0x80u) >> 4) |
+                        ((be & 1u) << 2) | (b & 0x3u));
+  }
+}
+
+void lz_cpu_unpack_e5m2(const uint16_t* in, uint8_t* out, uint64_t npairs) {
+  for (uint64_t i = 0; i < npairs; ++i) {
+    const uint32_t w = in[i];
+    const uint32_t ae = (((w >> 11) & 0xF) << 1) | ((w >> 6) & 1);
+    const uint32_t be = (((w >> 7) & 0xF) << 1) | ((w >> 2) & 1);
+    out[2 * i] = (uint8_t)(((w >> 8) & 0x80u) | (ae << 2) | ((w >> 4) & 0x3u));
+    out[2 * i + 1] = (uint8_t)(((w << 4) & 0x80u) | (be << 2) | (w & 0x3u));
+  }
+}
+
+}  // extern "C"

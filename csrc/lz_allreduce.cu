@@ -511,6 +511,27 @@ __global__ void __launch_bounds__(512) ar_emu_kernel(const LzDevComm* cs, const 
 
 __global__ void read_epoch_kernel(LzDevComm c, unsigned long long* out) { *out = *c.epoch; }
 
+// World size 1: the allreduce is the identity; out-of-place calls copy with
+// 16-byte vectors (tail bytes by the first threads).
+__global__ void __launch_bounds__(512) local_copy_kernel(const char* __restrict__ in,
+                                                         char* __restrict__ out, size_t bytes) {
+  const size_t nv = bytes / 16;
+  const uint4* src = reinterpret_cast<const uint4*>(in);
+  uint4* dst = reinterpret_cast<uint4*>(out);
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < nv; i += 4 * stride) {
+    uint4 a = ld_nc_v4(src + i), b = ld_nc_v4(src + i + stride), c = ld_nc_v4(src + i + 2 * stride),
+          d = ld_nc_v4(src + i + 3 * stride);
+    st_cs_v4(dst + i, a);
+    st_cs_v4(dst + i + stride, b);
+    st_cs_v4(dst + i + 2 * stride, c);
+    st_cs_v4(dst + i + 3 * stride, d);
+  }
+  for (; i < nv; i += stride) st_cs_v4(dst + i, ld_nc_v4(src + i));
+  if (blockIdx.x == 0 && threadIdx.x < bytes - nv * 16) out[nv * 16 + threadIdx.x] = in[nv * 16 + threadIdx.x];
+}
+
 // ----------------------------------------------------------------------------
 // host side
 // ----------------------------------------------------------------------------
@@ -827,7 +848,17 @@ extern "C" int lz_allreduce(LzComm* c, const void* in, void* out, size_t count, 
                             int algo, int nblocks, int nthreads, cudaStream_t s) {
   if (c->dev.world == 1) {
     const size_t es = dtype == LZ_F32 ? 4 : 2;
-    if (in != out) LZ_CUDA_TRY(cudaMemcpyAsync(out, in, count * es, cudaMemcpyDeviceToDevice, s));
+    const size_t bytes = count * es;
+    if (in != out && bytes) {
+      const bool al = ((uintptr_t)in % 16 == 0) && ((uintptr_t)out % 16 == 0);
+      if (!al) {
+        LZ_CUDA_TRY(cudaMemcpyAsync(out, in, bytes, cudaMemcpyDeviceToDevice, s));
+      } else {
+        int G = clamp_int((long long)((bytes / 16 + 2047) / 2048), 1, c->sm_count * 4);
+        local_copy_kernel<<<G, 512, 0, s>>>(static_cast<const char*>(in), static_cast<char*>(out), bytes);
+        LZ_CUDA_TRY(cudaGetLastError());
+      }
+    }
     return LZE_OK;
   }
   ArPlan P;

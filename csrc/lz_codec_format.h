@@ -1,0 +1,225 @@
+// LZC1: lossless float codec format shared by the GPU kernels and the CPU
+// oracle (which must produce bit-identical streams).
+//
+// Split: every element is cut into a one-byte "symbol" (the exponent byte for
+// bf16/fp32, the high byte for fp16, the whole byte for 8-bit types) and a
+// "raw" remainder (sign + mantissa bits) that is stored verbatim. Only the
+// symbol plane is entropy coded. This is the split described by the
+// reference's UCCL logs (raw/bf16_split_sm16_split_encode_time_count.txt) and
+// dietgpu's float mode; the stream format and coder here are this project's own.
+//
+// Coder: rANS (J. Duda, "Asymmetric numeral systems", 2013) with 32-bit
+// states, 16-bit renormalisation words and PROB_BITS-bit quantised
+// frequencies, interleaved over the 32 lanes of a warp (the interleaving
+// scheme published by F. Giesen, "Interleaved entropy coders", 2014):
+// lane l codes symbols l, l+32, l+64, ... of its sub-block and all lanes share
+// one word stream whose per-step order is the lane order.
+//
+// Layout of one table group (TG, up to TG_ELEMS elements, own frequency table):
+//   TgHeader (32 B)
+//   raw plane: n * raw_bytes_per_elem(dtype), zero padded to 16 B
+//   symbol section, one of
+//     RAW  : n symbol bytes, padded to 16 B
+//     ANS  : table   nnz x u32 (sym << 16 | freq), padded to 16 B
+//            sizes   nsub x u32 (bytes of each sub-stream before padding), padded to 16 B
+//            nsub sub-streams, each: 32 x u32 final lane states, then the
+//            16-bit words in emission order, padded to 16 B.
+// A TG is coded ANS only if no sub-stream exceeds its sub-block's symbol
+// count in bytes (before padding) and the ANS section is smaller than the RAW
+// section; otherwise it is RAW. Decoding validates the magic, the sizes, that
+// every word was consumed and that every lane state returned to RANS_L.
+//
+// Whole-tensor stream ("compact" form):
+//   StreamHeader (64 B) | n_tg x u64 TG offsets (from stream start), padded to 16 B | TG records
+// Slotted form (fused transfer paths): TG t lives at t * tg_capacity().
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __CUDACC__
+#define LZC_HD __host__ __device__ __forceinline__
+#else
+#define LZC_HD inline
+#endif
+
+namespace lzc {
+
+constexpr uint32_t PROB_BITS = 11;
+constexpr uint32_t PROB_SCALE = 1u << PROB_BITS;
+constexpr uint32_t RANS_L = 1u << 16;
+constexpr int LANES = 32;
+constexpr int SUB_STEPS = 256;
+constexpr uint32_t SUB_ELEMS = LANES * SUB_STEPS;  // 8192
+constexpr int NSUB = 4;
+constexpr uint32_t TG_ELEMS = SUB_ELEMS * NSUB;    // 32768
+constexpr uint32_t TG_MAGIC = 0x47545A4Cu;         // "LZTG"
+constexpr uint32_t STREAM_MAGIC = 0x31435A4Cu;     // "LZC1"
+constexpr uint16_t VERSION = 1;
+constexpr uint8_t MODE_RAW = 0;
+constexpr uint8_t MODE_ANS = 1;
+
+// dtype codes (same values as LzDtype)
+constexpr int DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2, DT_U8 = 3;
+
+struct TgHeader {
+  uint32_t magic;
+  uint16_t version;
+  uint8_t mode;
+  uint8_t dtype;
+  uint32_t n;          // elements in this TG
+  uint32_t sym_bytes;  // bytes of the symbol section (padded)
+  uint32_t raw_bytes;  // bytes of the raw plane (padded)
+  uint16_t nnz;        // table entries (ANS)
+  uint16_t nsub;       // sub-streams (ANS)
+  uint32_t total;      // bytes of the whole record
+  uint32_t reserved;
+};
+static_assert(sizeof(TgHeader) == 32, "TgHeader must be 32 bytes");
+
+struct StreamHeader {
+  uint32_t magic;
+  uint16_t version;
+  uint8_t dtype;
+  uint8_t flags;
+  uint32_t tg_elems;
+  uint32_t n_tg;
+  uint64_t n_elems;
+  uint64_t total_bytes;
+  uint64_t reserved[4];
+};
+static_assert(sizeof(StreamHeader) == 64, "StreamHeader must be 64 bytes");
+
+LZC_HD uint32_t pad16(uint32_t x) { return (x + 15u) & ~15u; }
+LZC_HD uint64_t pad16_64(uint64_t x) { return (x + 15u) & ~uint64_t(15); }
+
+LZC_HD int elem_bytes(int dt) { return dt == DT_F32 ? 4 : (dt == DT_U8 ? 1 : 2); }
+LZC_HD int raw_bytes_per_elem(int dt) { return dt == DT_F32 ? 3 : (dt == DT_U8 ? 0 : 1); }
+
+// Worst-case record size of a TG of n elements (RAW symbol section).
+LZC_HD uint32_t tg_capacity_n(uint32_t n, int dt) {
+  return (uint32_t)sizeof(TgHeader) + pad16(n * (uint32_t)raw_bytes_per_elem(dt)) + pad16(n);
+}
+LZC_HD uint32_t tg_capacity(int dt) { return tg_capacity_n(TG_ELEMS, dt); }
+
+LZC_HD uint64_t num_tgs(uint64_t n) { return (n + TG_ELEMS - 1) / TG_ELEMS; }
+
+LZC_HD uint64_t max_stream_bytes(uint64_t n, int dt) {
+  const uint64_t ntg = num_tgs(n);
+  return sizeof(StreamHeader) + pad16_64(8 * ntg) + ntg * (uint64_t)tg_capacity(dt);
+}
+
+// --- split / merge of one element -------------------------------------------
+// bf16: symbol = exponent byte (bits 14..7); raw = sign << 7 | mantissa(7).
+// fp16: symbol = high byte (sign, exponent, 2 mantissa bits); raw = low byte.
+// fp32: symbol = exponent byte (bits 30..23); raw = sign << 23 | mantissa(23), 3 bytes LE.
+// u8  : symbol = the byte; no raw plane.
+LZC_HD uint8_t sym_bf16(uint16_t u) { return (uint8_t)((u >> 7) & 0xFF); }
+LZC_HD uint8_t raw_bf16(uint16_t u) { return (uint8_t)(((u >> 8) & 0x80) | (u & 0x7F)); }
+LZC_HD uint16_t merge_bf16(uint8_t s, uint8_t r) {
+  return (uint16_t)(((uint16_t)(r & 0x80) << 8) | ((uint16_t)s << 7) | (r & 0x7F));
+}
+LZC_HD uint8_t sym_f16(uint16_t u) { return (uint8_t)(u >> 8); }
+LZC_HD uint8_t raw_f16(uint16_t u) { return (uint8_t)(u & 0xFF); }
+LZC_HD uint16_t merge_f16(uint8_t s, uint8_t r) { return (uint16_t)(((uint16_t)s << 8) | r); }
+LZC_HD uint8_t sym_f32(uint32_t u) { return (uint8_t)((u >> 23) & 0xFF); }
+LZC_HD uint32_t raw_f32(uint32_t u) { return (u & 0x7FFFFFu) | ((u >> 31) << 23); }
+LZC_HD uint32_t merge_f32(uint8_t s, uint32_t r) {
+  return ((r >> 23) << 31) | ((uint32_t)s << 23) | (r & 0x7FFFFFu);
+}
+
+// --- frequency normalisation (must be identical on CPU and GPU) -------------
+// counts[256] of `total` symbols -> freq[256] summing to PROB_SCALE, every
+// present symbol >= 1. Surplus goes to / deficit comes from the symbol with
+// the largest count / frequency (ties: smallest symbol).
+LZC_HD void normalize_freqs(const uint32_t* counts, uint32_t total, uint32_t* freq) {
+  uint32_t sum = 0;
+  int argmax_c = -1;
+  uint32_t maxc = 0;
+  for (int s = 0; s < 256; ++s) {
+    uint32_t c = counts[s];
+    uint32_t f = 0;
+    if (c) {
+      f = (uint32_t)(((uint64_t)c * PROB_SCALE) / total);
+      if (f == 0) f = 1;
+      if (c > maxc) {
+        maxc = c;
+        argmax_c = s;
+      }
+    }
+    freq[s] = f;
+    sum += f;
+  }
+  if (argmax_c < 0) return;
+  if (sum < PROB_SCALE) {
+    freq[argmax_c] += PROB_SCALE - sum;
+    return;
+  }
+  while (sum > PROB_SCALE) {
+    int best = -1;
+    uint32_t bf = 1;
+    for (int s = 0; s < 256; ++s) {
+      if (freq[s] > bf) {
+        bf = freq[s];
+        best = s;
+      }
+    }
+    uint32_t d = sum - PROB_SCALE;
+    if (d > bf - 1) d = bf - 1;
+    freq[best] -= d;
+    sum -= d;
+  }
+}
+
+// floor(x / f) without a divide: m = ceil(2^(32+l) / f) with l = ceil(log2 f),
+// stored as m - 2^32 (< 2^32); q = (x + umulhi(x, m_lo)) >> l. Exact for all
+// 32-bit x because f <= 2^l. (Granlund & Montgomery, "Division by invariant
+// integers using multiplication", PLDI 1994.)
+struct EncSym {
+  uint32_t m_lo;
+  uint32_t freq;
+  uint32_t cum;
+  uint32_t shift;
+};
+
+LZC_HD EncSym make_enc_sym(uint32_t f, uint32_t cum) {
+  EncSym e;
+  e.freq = f;
+  e.cum = cum;
+  uint32_t l = 0;
+  while ((1u << l) < f) ++l;
+  e.shift = l;
+  const uint64_t m = ((uint64_t(1) << (32 + l)) + f - 1) / f;
+  e.m_lo = (uint32_t)(m - (uint64_t(1) << 32));
+  return e;
+}
+
+LZC_HD uint32_t umulhi32(uint32_t a, uint32_t b) {
+#ifdef __CUDA_ARCH__
+  return __umulhi(a, b);
+#else
+  return (uint32_t)(((uint64_t)a * b) >> 32);
+#endif
+}
+
+// One rANS encode step: returns true (and the word) if a renormalisation word
+// must be emitted before the state update.
+LZC_HD bool enc_needs_word(uint32_t x, uint32_t f) {
+  return (uint64_t)x >= ((uint64_t)f << (32 - PROB_BITS));
+}
+LZC_HD uint32_t enc_update(uint32_t x, const EncSym& e) {
+  const uint32_t q = (uint32_t)(((uint64_t)x + umulhi32(x, e.m_lo)) >> e.shift);
+  const uint32_t r = x - q * e.freq;
+  return (q << PROB_BITS) + r + e.cum;
+}
+
+// Decode table entry for a slot: sym | (freq-1) << 8 | (slot - cum) << 20.
+LZC_HD uint32_t dec_entry(uint32_t sym, uint32_t freq, uint32_t bias) {
+  return sym | ((freq - 1u) << 8) | (bias << 20);
+}
+LZC_HD uint32_t dec_update(uint32_t x, uint32_t entry) {
+  const uint32_t f = ((entry >> 8) & 0xFFFu) + 1u;
+  const uint32_t bias = entry >> 20;
+  return f * (x >> PROB_BITS) + bias;
+}
+
+}  // namespace lzc

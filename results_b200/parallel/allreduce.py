@@ -1,0 +1,79 @@
+"""Public allreduce entry point with per-size algorithm selection.
+
+``allreduce(t, algo=...)`` covers every variant of the reference's
+benchmark driver (single_node_nccl_allreduce_benchmark/benchmark_both.py:372-383,
+16_node_nccl_allreduce_benchmark/benchmark_both.py:156-176):
+
+* native sm_100a kernels over NVLink peer memory / NVLS (CUDA tensors):
+  ``oneshot``, ``twoshot`` (alias ``p2p``), ``nvls``, ``nvls_oneshot``,
+  ``ring`` (alias ``ringp2p``), ``rhd``;
+* NCCL baseline: ``nccl`` (``dist.all_reduce``);
+* host-orchestrated send/recv reference algorithms (any backend, also CPU):
+  ``naive``, ``naive_twoshot``, ``ring_sendrecv``, ``rhd_sendrecv``,
+  ``twoshot_collective``, ``multichannel_ring``, ``hierarchical``;
+* ``auto``: the measured size table of :mod:`results_b200.parallel.tuning`.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..config import Config
+from .comm import Communicator
+
+_DEFAULT: Communicator | None = None
+
+NATIVE = {"oneshot", "twoshot", "nvls", "nvls_oneshot", "ring", "rhd"}
+ALIASES = {"p2p": "twoshot", "ringp2p": "ring", "two_shot": "twoshot", "one_shot": "oneshot"}
+HOST_ALGOS = {"naive", "naive_twoshot", "ring_sendrecv", "rhd_sendrecv", "twoshot_collective",
+              "multichannel_ring", "hierarchical", "pipelined_twoshot"}
+
+
+def init(group=None, config: Config | None = None) -> Communicator:
+    """Create (collectively) the default communicator for ``group``."""
+    global _DEFAULT
+    if _DEFAULT is None:
+        _DEFAULT = Communicator(group=group, config=config)
+    return _DEFAULT
+
+
+def get_comm() -> Communicator | None:
+    return _DEFAULT
+
+
+def shutdown() -> None:
+    global _DEFAULT
+    if _DEFAULT is not None:
+        _DEFAULT.close()
+        _DEFAULT = None
+
+
+def select_algo(nbytes: int, world: int, has_multicast: bool, symmetric: bool,
+                config: Config | None = None) -> str:
+    from .tuning import choose
+
+    return choose(nbytes, world, has_multicast, symmetric)
+
+
+def allreduce(t: torch.Tensor, algo: str = "auto", out: torch.Tensor | None = None,
+              comm: Communicator | None = None, group=None) -> torch.Tensor:
+    """Sum-allreduce ``t`` across the group. In place unless ``out`` is given."""
+    algo = ALIASES.get(algo, algo)
+    if algo == "nccl" or (not t.is_cuda and algo in ("auto", "nccl")):
+        res = t if out is None else out.copy_(t)
+        dist.all_reduce(res, op=dist.ReduceOp.SUM, group=group)
+        return res
+    if algo in HOST_ALGOS:
+        from . import sendrecv
+
+        res = t if out is None else out.copy_(t)
+        sendrecv.allreduce(res, algo, group=group)
+        return res
+    comm = comm or _DEFAULT or init(group)
+    if algo == "auto":
+        algo = select_algo(t.numel() * t.element_size(), comm.world, comm.has_multicast,
+                           comm.is_symmetric(t) and (out is None or comm.is_symmetric(out)),
+                           comm.config)
+    if algo not in NATIVE:
+        raise ValueError(f"unknown allreduce algorithm {algo!r}")
+    return comm.allreduce_(t, out, algo=algo)
