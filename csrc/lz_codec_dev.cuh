@@ -1,0 +1,574 @@
+// Device-side LZC1 table-group (TG) encoder and decoder, used by the
+// standalone codec kernels (lz_codec.cu) and by the fused transfer kernels
+// (compressed allreduce, weight transfer), which write/read records directly
+// in peer or multicast memory.
+//
+// One CTA of LZC_THREADS = 4 warps handles one TG (4 sub-blocks of 8192
+// symbols, one warp per sub-block). Output is bit-identical to the CPU oracle
+// (csrc/cpu/lz_cpu.cpp).
+#pragma once
+#include "lz_codec_format.h"
+#include "lz_common.cuh"
+
+namespace lzg {
+
+using namespace lzc;
+constexpr int LZC_THREADS = 128;
+static_assert(LZC_THREADS / 32 == NSUB, "one warp per sub-block");
+
+struct EncSmem {
+  uint8_t syms[TG_ELEMS];  // symbol plane of the TG
+  union {
+    uint8_t streams[NSUB][SUB_ELEMS];  // per-warp rANS output (states + words)
+    uint32_t counts[NSUB][256];        // per-warp histograms (before encoding)
+  } u;
+  EncSym tab[256];
+  uint32_t table[256];
+  uint32_t sub_len[NSUB];
+  uint32_t nnz;
+  uint32_t total;
+};
+
+struct DecSmem {
+  uint32_t dtab[PROB_SCALE];
+  uint8_t syms[TG_ELEMS];
+  TgHeader h;
+  int ok;
+};
+
+LZ_DEV uint32_t lane_id() { return threadIdx.x & 31; }
+LZ_DEV uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// ---------------------------------------------------------------------------
+// split of 16 elements (one "unit") starting at element index e
+// ---------------------------------------------------------------------------
+template <int DT>
+struct Split16;
+
+template <>
+struct Split16<DT_BF16> {
+  static constexpr int IN_VECS = 2, RAW_BYTES = 16;
+  LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t* raw) {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(v);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      sym[k] = sym_bf16(h[k]);
+      raw[k] = raw_bf16(h[k]);
+    }
+  }
+  LZ_DEV static void merge(const uint8_t* sym, const uint8_t* raw, uint4* v) {
+    uint16_t* h = reinterpret_cast<uint16_t*>(v);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) h[k] = merge_bf16(sym[k], raw[k]);
+  }
+};
+template <>
+struct Split16<DT_F16> {
+  static constexpr int IN_VECS = 2, RAW_BYTES = 16;
+  LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t* raw) {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(v);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      sym[k] = sym_f16(h[k]);
+      raw[k] = raw_f16(h[k]);
+    }
+  }
+  LZ_DEV static void merge(const uint8_t* sym, const uint8_t* raw, uint4* v) {
+    uint16_t* h = reinterpret_cast<uint16_t*>(v);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) h[k] = merge_f16(sym[k], raw[k]);
+  }
+};
+template <>
+struct Split16<DT_F32> {
+  static constexpr int IN_VECS = 4, RAW_BYTES = 48;
+  LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t* raw) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(v);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      sym[k] = sym_f32(w[k]);
+      const uint32_t r = raw_f32(w[k]);
+      raw[3 * k] = (uint8_t)r;
+      raw[3 * k + 1] = (uint8_t)(r >> 8);
+      raw[3 * k + 2] = (uint8_t)(r >> 16);
+    }
+  }
+  LZ_DEV static void merge(const uint8_t* sym, const uint8_t* raw, uint4* v) {
+    uint32_t* w = reinterpret_cast<uint32_t*>(v);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint32_t r = raw[3 * k] | ((uint32_t)raw[3 * k + 1] << 8) | ((uint32_t)raw[3 * k + 2] << 16);
+      w[k] = merge_f32(sym[k], r);
+    }
+  }
+};
+template <>
+struct Split16<DT_U8> {
+  static constexpr int IN_VECS = 1, RAW_BYTES = 0;
+  LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t*) {
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(v);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) sym[k] = b[k];
+  }
+  LZ_DEV static void merge(const uint8_t* sym, const uint8_t*, uint4* v) {
+    uint8_t* b = reinterpret_cast<uint8_t*>(v);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) b[k] = sym[k];
+  }
+};
+
+// Scalar split/merge of element i (tails).
+template <int DT>
+LZ_DEV void split1(const char* in, uint32_t i, uint8_t* sym, uint8_t* raw) {
+  if (DT == DT_BF16) {
+    uint16_t u = reinterpret_cast<const uint16_t*>(in)[i];
+    *sym = sym_bf16(u);
+    raw[0] = raw_bf16(u);
+  } else if (DT == DT_F16) {
+    uint16_t u = reinterpret_cast<const uint16_t*>(in)[i];
+    *sym = sym_f16(u);
+    raw[0] = raw_f16(u);
+  } else if (DT == DT_F32) {
+    uint32_t u = reinterpret_cast<const uint32_t*>(in)[i];
+    *sym = sym_f32(u);
+    uint32_t r = raw_f32(u);
+    raw[0] = (uint8_t)r;
+    raw[1] = (uint8_t)(r >> 8);
+    raw[2] = (uint8_t)(r >> 16);
+  } else {
+    *sym = reinterpret_cast<const uint8_t*>(in)[i];
+  }
+}
+
+template <int DT>
+LZ_DEV void merge1(char* out, uint32_t i, uint8_t sym, const uint8_t* raw) {
+  if (DT == DT_BF16) {
+    reinterpret_cast<uint16_t*>(out)[i] = merge_bf16(sym, raw[0]);
+  } else if (DT == DT_F16) {
+    reinterpret_cast<uint16_t*>(out)[i] = merge_f16(sym, raw[0]);
+  } else if (DT == DT_F32) {
+    uint32_t r = raw[0] | ((uint32_t)raw[1] << 8) | ((uint32_t)raw[2] << 16);
+    reinterpret_cast<uint32_t*>(out)[i] = merge_f32(sym, r);
+  } else {
+    reinterpret_cast<uint8_t*>(out)[i] = sym;
+  }
+}
+
+// Copies `bytes` (multiple of 16, both 16-B aligned) with the whole CTA.
+LZ_DEV void cta_copy16(char* dst, const char* src, uint32_t bytes) {
+  for (uint32_t o = threadIdx.x * 16; o < bytes; o += blockDim.x * 16)
+    st_v4(dst + o, *reinterpret_cast<const uint4*>(src + o));
+}
+
+// ---------------------------------------------------------------------------
+// Frequency table (warp 0): counts -> freq -> cumulative -> encoder table and
+// the compact list of (sym << 16 | freq). Same result as normalize_freqs().
+// ---------------------------------------------------------------------------
+LZ_DEV void build_tables_warp0(EncSmem& sm, uint32_t n) {
+  const uint32_t lane = lane_id();
+  uint32_t c[8], f[8];
+  uint32_t sum = 0, maxc = 0;
+  int argmax = 256;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int s = lane * 8 + k;
+    c[k] = sm.u.counts[0][s] + sm.u.counts[1][s] + sm.u.counts[2][s] + sm.u.counts[3][s];
+    f[k] = 0;
+    if (c[k]) {
+      f[k] = (uint32_t)(((uint64_t)c[k] * PROB_SCALE) / n);
+      if (f[k] == 0) f[k] = 1;
+      if (c[k] > maxc) {
+        maxc = c[k];
+        argmax = s;
+      }
+    }
+    sum += f[k];
+  }
+  // warp reductions: total, and (max count, smallest symbol)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    uint32_t oc = __shfl_xor_sync(0xffffffffu, maxc, o);
+    int oa = __shfl_xor_sync(0xffffffffu, argmax, o);
+    if (oc > maxc || (oc == maxc && oa < argmax)) {
+      maxc = oc;
+      argmax = oa;
+    }
+  }
+  if (maxc > 0) {
+    if (sum < PROB_SCALE) {
+      if (argmax / 8 == (int)lane) f[argmax % 8] += PROB_SCALE - sum;
+    } else {
+      while (sum > PROB_SCALE) {  // rare: take the excess from the largest frequency
+        uint32_t bf = 1;
+        int best = 256;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (f[k] > bf) {
+            bf = f[k];
+            best = lane * 8 + k;
+          }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          uint32_t ob = __shfl_xor_sync(0xffffffffu, bf, o);
+          int os = __shfl_xor_sync(0xffffffffu, best, o);
+          if (ob > bf || (ob == bf && os < best)) {
+            bf = ob;
+            best = os;
+          }
+        }
+        uint32_t d = sum - PROB_SCALE;
+        if (d > bf - 1) d = bf - 1;
+        if (best / 8 == (int)lane) f[best % 8] -= d;
+        sum -= d;
+      }
+    }
+  }
+  // exclusive prefix over symbols (8 per lane, lanes in order)
+  uint32_t lsum = 0, lnz = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    lsum += f[k];
+    lnz += f[k] ? 1u : 0u;
+  }
+  uint32_t incl = lsum, inz = lnz;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t a = __shfl_up_sync(0xffffffffu, incl, o);
+    uint32_t b = __shfl_up_sync(0xffffffffu, inz, o);
+    if (lane >= (uint32_t)o) {
+      incl += a;
+      inz += b;
+    }
+  }
+  uint32_t cum = incl - lsum, pos = inz - lnz;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int s = lane * 8 + k;
+    sm.tab[s] = make_enc_sym(f[k] ? f[k] : 1, cum);
+    if (f[k]) sm.table[pos++] = ((uint32_t)s << 16) | f[k];
+    cum += f[k];
+  }
+  if (lane == 31) sm.nnz = inz;
+}
+
+// ---------------------------------------------------------------------------
+// Encode one TG of n elements from `in` (16-B aligned) into the record at
+// `dst` (16-B aligned; any memory the CTA can store to: local, peer).
+// Returns the record size (uniform over the CTA).
+// ---------------------------------------------------------------------------
+template <int DT>
+LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restrict__ dst,
+                          EncSmem& sm) {
+  using S = Split16<DT>;
+  constexpr int RB = DT == DT_F32 ? 3 : (DT == DT_U8 ? 0 : 1);
+  constexpr int ES = DT == DT_F32 ? 4 : (DT == DT_U8 ? 1 : 2);
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t raw_bytes = pad16(n * RB);
+  char* raw_dst = dst + sizeof(TgHeader);
+
+  for (uint32_t k = tid; k < NSUB * 256; k += blockDim.x) (&sm.u.counts[0][0])[k] = 0;
+  __syncthreads();
+  // 1. split + histogram (+ raw plane straight to the destination)
+  const uint32_t units = n / 16;
+  for (uint32_t u0 = 0; u0 < units; u0 += blockDim.x) {  // block-uniform trip count
+    const uint32_t u = u0 + tid;
+    const bool act = u < units;
+    uint8_t sy[16];
+    if (act) {
+      uint4 v[S::IN_VECS];
+#pragma unroll
+      for (int q = 0; q < S::IN_VECS; ++q)
+        v[q] = *reinterpret_cast<const uint4*>(in + (size_t)u * 16 * ES + 16 * q);
+      uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 1];
+      S::split(v, sy, rw);
+      *reinterpret_cast<uint4*>(&sm.syms[u * 16]) = *reinterpret_cast<const uint4*>(sy);
+      if (RB > 0) {
+#pragma unroll
+        for (int q = 0; q < S::RAW_BYTES / 16; ++q)
+          st_v4(raw_dst + (size_t)u * S::RAW_BYTES + 16 * q, reinterpret_cast<const uint4*>(rw)[q]);
+      }
+    }
+    // warp-aggregated histogram: one shared atomic per distinct symbol
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint32_t key = act ? (uint32_t)sy[k] : 256u + lane;
+      const uint32_t peers = __match_any_sync(0xffffffffu, key);
+      if (act && (__ffs(peers) - 1) == (int)lane) atomicAdd(&sm.u.counts[warp][sy[k]], __popc(peers));
+    }
+  }
+  // tail elements (n % 16) and the zero padding of the raw plane
+  if (tid < n - units * 16) {
+    const uint32_t i = units * 16 + tid;
+    uint8_t s1, r1[4];
+    split1<DT>(in, i, &s1, r1);
+    sm.syms[i] = s1;
+    atomicAdd(&sm.u.counts[0][s1], 1u);
+    for (int q = 0; q < RB; ++q) raw_dst[(size_t)i * RB + q] = (char)r1[q];
+  }
+  if (RB > 0 && tid < raw_bytes - n * RB) raw_dst[n * RB + tid] = 0;
+  __syncthreads();
+  // 2. frequency tables
+  if (warp == 0) build_tables_warp0(sm, n);
+  __syncthreads();
+  // 3. one warp per sub-block: interleaved rANS, backward over the steps
+  const uint32_t nsub = (n + SUB_ELEMS - 1) / SUB_ELEMS;
+  if (warp < nsub) {
+    const uint32_t base = warp * SUB_ELEMS;
+    const uint32_t sn = min(SUB_ELEMS, n - base);
+    uint8_t* out = sm.u.streams[warp];
+    uint32_t x = RANS_L;
+    uint32_t pos = 0;  // words emitted (warp-uniform)
+    bool overflow = false;
+    const int jmax = (int)((sn + LANES - 1) / LANES) - 1;
+    const uint32_t lt = lanemask_lt();
+    for (int j = jmax; j >= 0; --j) {
+      const uint32_t i = (uint32_t)j * LANES + lane;
+      const bool act = i < sn;
+      EncSym e;
+      if (act) e = sm.tab[sm.syms[base + i]];
+      const bool need = act && enc_needs_word(x, e.freq);
+      const uint32_t m = __ballot_sync(0xffffffffu, need);
+      const uint32_t cnt = __popc(m);
+      if (128u + 2u * (pos + cnt) > sn) {
+        overflow = true;
+        break;
+      }
+      if (need) {
+        *reinterpret_cast<uint16_t*>(out + 128 + 2 * (pos + __popc(m & lt))) = (uint16_t)(x & 0xFFFF);
+        x >>= 16;
+      }
+      pos += cnt;
+      if (act) x = enc_update(x, e);
+    }
+    if (!overflow) {
+      reinterpret_cast<uint32_t*>(out)[lane] = x;
+      // zero the padding words so records are deterministic
+      const uint32_t len = 128u + 2u * pos;
+      if (lane < (pad16(len) - len) / 2) *reinterpret_cast<uint16_t*>(out + len + 2 * lane) = 0;
+    }
+    if (lane == 0) sm.sub_len[warp] = overflow ? 0u : 128u + 2u * pos;
+  }
+  __syncthreads();
+  // 4. mode decision and record emission
+  __shared__ uint32_t s_mode, s_symbytes, s_tabbytes;
+  if (tid == 0) {
+    bool ans = n > 0;
+    uint32_t bytes = pad16(4 * sm.nnz) + pad16(4 * nsub);
+    for (uint32_t b = 0; b < nsub; ++b) {
+      if (sm.sub_len[b] == 0) ans = false;
+      bytes += pad16(sm.sub_len[b]);
+    }
+    if (bytes >= pad16(n)) ans = false;
+    s_mode = ans ? MODE_ANS : MODE_RAW;
+    s_symbytes = ans ? bytes : pad16(n);
+    s_tabbytes = pad16(4 * sm.nnz);
+    TgHeader h;
+    h.magic = TG_MAGIC;
+    h.version = VERSION;
+    h.mode = (uint8_t)s_mode;
+    h.dtype = (uint8_t)DT;
+    h.n = n;
+    h.sym_bytes = s_symbytes;
+    h.raw_bytes = raw_bytes;
+    h.nnz = ans ? (uint16_t)sm.nnz : 0;
+    h.nsub = ans ? (uint16_t)nsub : 0;
+    h.total = (uint32_t)sizeof(TgHeader) + raw_bytes + s_symbytes;
+    h.reserved = 0;
+    const uint4* hv = reinterpret_cast<const uint4*>(&h);
+    st_v4(dst, hv[0]);
+    st_v4(dst + 16, hv[1]);
+    sm.total = h.total;
+  }
+  __syncthreads();
+  char* symsec = raw_dst + raw_bytes;
+  if (s_mode == MODE_RAW) {
+    // zero the padding of the symbol plane, then copy it
+    if (tid < pad16(n) - n) sm.syms[n + tid] = 0;
+    __syncthreads();
+    cta_copy16(symsec, reinterpret_cast<const char*>(sm.syms), pad16(n));
+  } else {
+    const uint32_t tb = s_tabbytes;
+    for (uint32_t k = tid; k < tb / 4; k += blockDim.x)
+      reinterpret_cast<uint32_t*>(symsec)[k] = k < sm.nnz ? sm.table[k] : 0u;
+    const uint32_t sb = pad16(4 * nsub);
+    if (tid < sb / 4) reinterpret_cast<uint32_t*>(symsec + tb)[tid] = tid < nsub ? sm.sub_len[tid] : 0u;
+    uint32_t off = tb + sb;
+    for (uint32_t b = 0; b < nsub; ++b) {
+      const uint32_t len = pad16(sm.sub_len[b]);
+      cta_copy16(symsec + off, reinterpret_cast<const char*>(sm.u.streams[b]), len);
+      off += len;
+    }
+  }
+  const uint32_t total = sm.total;
+  __syncthreads();
+  return total;
+}
+
+// ---------------------------------------------------------------------------
+// Decode one TG record at `src` (n elements expected) into `out`.
+// Returns true on success (uniform over the CTA); on a corrupt record nothing
+// beyond `out[0, n)` is written and false is returned.
+// ---------------------------------------------------------------------------
+template <int DT>
+LZ_DEV bool decode_tg(const char* __restrict__ src, uint32_t cap, uint32_t n, char* __restrict__ out,
+                      DecSmem& sm) {
+  using S = Split16<DT>;
+  constexpr int RB = DT == DT_F32 ? 3 : (DT == DT_U8 ? 0 : 1);
+  constexpr int ES = DT == DT_F32 ? 4 : (DT == DT_U8 ? 1 : 2);
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    TgHeader h;
+    uint4* hv = reinterpret_cast<uint4*>(&h);
+    hv[0] = ld_cg_v4(src);
+    hv[1] = ld_cg_v4(src + 16);
+    int ok = h.magic == TG_MAGIC && h.version == VERSION && h.dtype == DT && h.n == n &&
+             h.raw_bytes == pad16(n * RB) && h.total <= cap &&
+             h.total == sizeof(TgHeader) + h.raw_bytes + h.sym_bytes;
+    if (ok && h.mode == MODE_RAW) ok = h.sym_bytes == pad16(n);
+    else if (ok && h.mode == MODE_ANS)
+      ok = h.nsub == (n + SUB_ELEMS - 1) / SUB_ELEMS && h.nnz >= 1 && h.nnz <= 256 &&
+           pad16(4u * h.nnz) + pad16(4u * h.nsub) <= h.sym_bytes;
+    else ok = 0;
+    sm.h = h;
+    sm.ok = ok;
+  }
+  __syncthreads();
+  if (!sm.ok) return false;
+  const char* raw = src + sizeof(TgHeader);
+  const char* symsec = raw + sm.h.raw_bytes;
+  if (sm.h.mode == MODE_RAW) {
+    for (uint32_t o = tid * 16; o < pad16(n); o += blockDim.x * 16)
+      *reinterpret_cast<uint4*>(&sm.syms[o]) = ld_cg_v4(symsec + o);
+  } else {
+    const uint32_t nnz = sm.h.nnz, nsub = sm.h.nsub;
+    // decode table: slot -> entry, by binary search over the cumulative table
+    __shared__ uint32_t s_cum[257];
+    __shared__ uint32_t s_ent[256];
+    if (warp == 0) {
+      uint32_t e[8], f[8], lsum = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t idx = lane * 8 + k;
+        e[k] = idx < nnz ? *reinterpret_cast<const uint32_t*>(symsec + 4 * idx) : 0u;
+        f[k] = e[k] & 0xFFFF;
+        lsum += f[k];
+      }
+      uint32_t incl = lsum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        uint32_t a = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= (uint32_t)o) incl += a;
+      }
+      uint32_t cum = incl - lsum;
+      int bad = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t idx = lane * 8 + k;
+        if (idx < nnz) {
+          s_cum[idx] = cum;
+          s_ent[idx] = e[k];
+          if (f[k] == 0 || (e[k] >> 16) > 255) bad = 1;
+        }
+        cum += f[k];
+      }
+      const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+      bad = __any_sync(0xffffffffu, bad);
+      if (lane == 0) {
+        s_cum[nnz] = PROB_SCALE;
+        if (bad || total != PROB_SCALE) sm.ok = 0;
+      }
+    }
+    __syncthreads();
+    if (!sm.ok) return false;
+    for (uint32_t slot = tid; slot < PROB_SCALE; slot += blockDim.x) {
+      uint32_t lo = 0, hi = nnz;  // find k with cum[k] <= slot < cum[k+1]
+      while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (s_cum[mid] <= slot) lo = mid;
+        else hi = mid;
+      }
+      const uint32_t ent = s_ent[lo];
+      sm.dtab[slot] = dec_entry(ent >> 16, ent & 0xFFFF, slot - s_cum[lo]);
+    }
+    __syncthreads();
+    // one warp per sub-stream
+    const char* sizes = symsec + pad16(4 * nnz);
+    uint32_t off = pad16(4 * nnz) + pad16(4 * nsub);
+    bool good = true;
+    for (uint32_t b = 0; b < nsub; ++b) {
+      const uint32_t len = *reinterpret_cast<const uint32_t*>(sizes + 4 * b);
+      if (len < 128 || (len & 1) || off + pad16(len) > sm.h.sym_bytes) {
+        good = false;
+        break;
+      }
+      if (b == warp) {
+        const char* st = symsec + off;
+        const uint32_t base = b * SUB_ELEMS;
+        const uint32_t sn = min(SUB_ELEMS, n - base);
+        uint32_t x = *reinterpret_cast<const uint32_t*>(st + 4 * lane);
+        const uint16_t* words = reinterpret_cast<const uint16_t*>(st + 128);
+        int E = (int)((len - 128) / 2);
+        const uint32_t lt = lanemask_lt();
+        const int jn = (int)((sn + LANES - 1) / LANES);
+        bool wok = true;
+        for (int j = 0; j < jn; ++j) {
+          const uint32_t i = (uint32_t)j * LANES + lane;
+          const bool act = i < sn;
+          bool need = false;
+          if (act) {
+            const uint32_t ent = sm.dtab[x & (PROB_SCALE - 1)];
+            sm.syms[base + i] = (uint8_t)(ent & 0xFF);
+            x = dec_update(x, ent);
+            need = x < RANS_L;
+          }
+          const uint32_t m = __ballot_sync(0xffffffffu, need);
+          const int k = __popc(m);
+          if (k > E) {
+            wok = false;
+            break;
+          }
+          if (need) x = (x << 16) | words[E - k + __popc(m & lt)];
+          E -= k;
+        }
+        wok = wok && E == 0 && x == RANS_L;
+        wok = __all_sync(0xffffffffu, wok);
+        if (!wok && lane == 0) sm.ok = 0;
+      }
+      off += pad16(len);
+    }
+    if (!good && tid == 0) sm.ok = 0;
+    __syncthreads();
+    if (!sm.ok) return false;
+  }
+  __syncthreads();
+  // merge symbols with the raw plane
+  const uint32_t units = n / 16;
+  for (uint32_t u = tid; u < units; u += blockDim.x) {
+    uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 16];
+#pragma unroll
+    for (int q = 0; q < S::RAW_BYTES / 16; ++q)
+      reinterpret_cast<uint4*>(rw)[q] = ld_cg_v4(raw + (size_t)u * S::RAW_BYTES + 16 * q);
+    uint4 sv = *reinterpret_cast<const uint4*>(&sm.syms[u * 16]);
+    uint4 v[S::IN_VECS];
+    S::merge(reinterpret_cast<const uint8_t*>(&sv), rw, v);
+#pragma unroll
+    for (int q = 0; q < S::IN_VECS; ++q)
+      st_v4(out + (size_t)u * 16 * ES + 16 * q, v[q]);
+  }
+  if (tid < n - units * 16) {
+    const uint32_t i = units * 16 + tid;
+    uint8_t r1[4] = {0, 0, 0, 0};
+    for (int q = 0; q < RB; ++q) r1[q] = (uint8_t)raw[(size_t)i * RB + q];
+    merge1<DT>(out, i, sm.syms[i], r1);
+  }
+  __syncthreads();
+  return true;
+}
+
+}  // namespace lzg

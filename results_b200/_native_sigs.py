@@ -24,21 +24,33 @@ _CUDA = {
 _CPU = {}
 
 
-def declare(lib, sig) -> None:
-    for name, (res, *args) in _CUDA.items():
+_LOADED = {"cuda": None, "cpu": None}
+
+
+def _apply(lib, table, sig) -> None:
+    for name, (res, *args) in table.items():
         if hasattr(lib, name):
             sig(lib, name, res, *args)
+
+
+def declare(lib, sig) -> None:
+    _LOADED["cuda"] = (lib, sig)
+    _apply(lib, _CUDA, sig)
 
 
 def declare_cpu(lib, sig) -> None:
-    for name, (res, *args) in _CPU.items():
-        if hasattr(lib, name):
-            sig(lib, name, res, *args)
+    _LOADED["cpu"] = (lib, sig)
+    _apply(lib, _CPU, sig)
 
 
 def add_cuda(table: dict) -> None:
+    """Register signatures; applied now if the library is already loaded."""
     _CUDA.update(table)
+    if _LOADED["cuda"] is not None:
+        _apply(_LOADED["cuda"][0], table, _LOADED["cuda"][1])
 
 
 def add_cpu(table: dict) -> None:
     _CPU.update(table)
+    if _LOADED["cpu"] is not None:
+        _apply(_LOADED["cpu"][0], table, _LOADED["cpu"][1])
