@@ -245,7 +245,7 @@ int lzc_tg_decode(const void* rec_, uint64_t rec_cap, void* out, uint32_t n, int
     memcpy(syms.data(), symsec, n);
   } else if (h.mode == MODE_ANS) {
     const uint32_t nsub = (n + SUB_ELEMS - 1) / SUB_ELEMS;
-    if (h.nsub != nsub || h.nnz == 0 || h.nnz > 256) return -6;
+    if (h.nsub != nsub || h.nnz == 0 || h.nnz > 256 || h.sym_bytes >= pad16(n)) return -6;
     const uint32_t tab_bytes = pad16(4u * h.nnz), sizes_bytes = pad16(4 * nsub);
     if (tab_bytes + sizes_bytes > h.sym_bytes) return -7;
     uint32_t dec_tab[PROB_SCALE];

@@ -32,6 +32,7 @@ struct EncSmem {
 struct DecSmem {
   uint32_t dtab[PROB_SCALE];
   uint8_t syms[TG_ELEMS];
+  uint8_t sec[TG_ELEMS];  // staged ANS symbol section (table, sizes, sub-streams)
   TgHeader h;
   int ok;
 };
@@ -250,8 +251,10 @@ LZ_DEV void build_tables_warp0(EncSmem& sm, uint32_t n) {
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int s = lane * 8 + k;
-    sm.tab[s] = make_enc_sym(f[k] ? f[k] : 1, cum);
-    if (f[k]) sm.table[pos++] = ((uint32_t)s << 16) | f[k];
+    if (f[k]) {
+      sm.tab[s] = make_enc_sym(f[k], cum);
+      sm.table[pos++] = ((uint32_t)s << 16) | f[k];
+    }
     cum += f[k];
   }
   if (lane == 31) sm.nnz = inz;
@@ -327,11 +330,17 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
     bool overflow = false;
     const int jmax = (int)((sn + LANES - 1) / LANES) - 1;
     const uint32_t lt = lanemask_lt();
+    // software-pipelined: the table entry of step j-1 is fetched while step j runs
+    EncSym e_next;
+    {
+      const uint32_t i0 = (uint32_t)jmax * LANES + lane;
+      if (jmax >= 0 && i0 < sn) e_next = sm.tab[sm.syms[base + i0]];
+    }
     for (int j = jmax; j >= 0; --j) {
       const uint32_t i = (uint32_t)j * LANES + lane;
       const bool act = i < sn;
-      EncSym e;
-      if (act) e = sm.tab[sm.syms[base + i]];
+      const EncSym e = e_next;
+      if (j > 0) e_next = sm.tab[sm.syms[base + i - LANES]];
       const bool need = act && enc_needs_word(x, e.freq);
       const uint32_t m = __ballot_sync(0xffffffffu, need);
       const uint32_t cnt = __popc(m);
@@ -433,6 +442,7 @@ LZ_DEV bool decode_tg(const char* __restrict__ src, uint32_t cap, uint32_t n, ch
     if (ok && h.mode == MODE_RAW) ok = h.sym_bytes == pad16(n);
     else if (ok && h.mode == MODE_ANS)
       ok = h.nsub == (n + SUB_ELEMS - 1) / SUB_ELEMS && h.nnz >= 1 && h.nnz <= 256 &&
+           h.sym_bytes < pad16(n) &&
            pad16(4u * h.nnz) + pad16(4u * h.nsub) <= h.sym_bytes;
     else ok = 0;
     sm.h = h;
@@ -441,12 +451,18 @@ LZ_DEV bool decode_tg(const char* __restrict__ src, uint32_t cap, uint32_t n, ch
   __syncthreads();
   if (!sm.ok) return false;
   const char* raw = src + sizeof(TgHeader);
-  const char* symsec = raw + sm.h.raw_bytes;
+  const char* symsec = raw + sm.h.raw_bytes;  // re-pointed at the staged copy for ANS
   if (sm.h.mode == MODE_RAW) {
     for (uint32_t o = tid * 16; o < pad16(n); o += blockDim.x * 16)
       *reinterpret_cast<uint4*>(&sm.syms[o]) = ld_cg_v4(symsec + o);
   } else {
     const uint32_t nnz = sm.h.nnz, nsub = sm.h.nsub;
+    // stage the whole ANS section (<= pad16(n) bytes) so every word fetch of
+    // the rANS loop is a shared-memory load, off the global-latency path
+    for (uint32_t o = tid * 16; o < sm.h.sym_bytes; o += blockDim.x * 16)
+      *reinterpret_cast<uint4*>(&sm.sec[o]) = ld_cg_v4(symsec + o);
+    __syncthreads();
+    symsec = reinterpret_cast<const char*>(sm.sec);
     // decode table: slot -> entry, by binary search over the cumulative table
     __shared__ uint32_t s_cum[257];
     __shared__ uint32_t s_ent[256];

@@ -1,0 +1,94 @@
+"""Send/recv reference algorithms on gloo CPU ranks, checked against
+torch.distributed.all_reduce (fp32 and bf16 at 1 KB, 1 MB
+and 64 MB, values N(0,1) from torch.manual_seed(0))."""
+import pytest
+import torch
+
+from tests._mp import run_ranks
+
+SIZES = {"1KB": 1 << 10, "1MB": 1 << 20, "64MB": 64 << 20}
+
+
+def _worker(rank, world, algos, sizes, dtypes, env_lws):
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    from results_b200.parallel import sendrecv
+
+    if env_lws:
+        os.environ["LOCAL_WORLD_SIZE"] = str(env_lws)
+    out = []
+    for dtname in dtypes:
+        dtype = getattr(torch, dtname)
+        es = torch.empty((), dtype=dtype).element_size()
+        for label in sizes:
+            n = SIZES[label] // es
+            torch.manual_seed(0)
+            xs = [torch.randn(n) for _ in range(world)]
+            ref = xs[rank].to(dtype).clone()
+            dist.all_reduce(ref)
+            exact = torch.stack([x.to(dtype).float() for x in xs]).sum(0)
+            for algo in algos:
+                if algo == "rhd_sendrecv" and world & (world - 1):
+                    continue
+                if algo in ("pipelined_twoshot", "naive_alloc") and world != 2:
+                    continue
+                t = xs[rank].to(dtype).clone()
+                sendrecv.allreduce(t, algo)
+                tol = 1e-4 if dtype == torch.float32 else 2.5e-2
+                err = ((t.float() - exact).abs().max() / exact.abs().max()).item()
+                err_nccl = ((t.float() - ref.float()).abs().max() / exact.abs().max()).item()
+                out.append((algo, dtname, label, err <= tol and err_nccl <= 2 * tol, err))
+    return out
+
+
+ALGOS = ["naive_twoshot", "ring_sendrecv", "rhd_sendrecv", "twoshot_collective", "multichannel_ring",
+         "pipelined_twoshot", "naive_alloc", "hierarchical"]
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_algorithms_small(world):
+    res = run_ranks(_worker, world, backend="gloo",
+                    args=(ALGOS, ["1KB", "1MB"], ["float32", "bfloat16"], None), timeout=300)
+    bad = [r for rr in res for r in rr if not r[3]]
+    assert not bad, bad
+    assert len(res[0]) > 0
+
+
+def test_algorithms_64mb_world2():
+    """BASELINE config 1 at the 64 MB size: ring, two-shot and RHD."""
+    res = run_ranks(_worker, 2, backend="gloo",
+                    args=(["ring_sendrecv", "naive_twoshot", "rhd_sendrecv", "twoshot_collective"],
+                          ["64MB"], ["float32", "bfloat16"], None), timeout=600)
+    bad = [r for rr in res for r in rr if not r[3]]
+    assert not bad, bad
+
+
+def test_hierarchical_two_fake_nodes():
+    """4 ranks as 2 'nodes' of 2 (LOCAL_WORLD_SIZE=2): serial and pipelined paths."""
+    res = run_ranks(_worker, 4, backend="gloo",
+                    args=(["hierarchical"], ["1KB", "64MB"], ["float32"], 2), timeout=600,
+                    env={"LZ_PIPELINE_MIN_ELEMENTS": str(1 << 20)})
+    bad = [r for rr in res for r in rr if not r[3]]
+    assert not bad, bad
+
+
+def _verify_worker(rank, world):
+    from results_b200.parallel import sendrecv
+
+    return all(sendrecv.verify_correctness(sendrecv.ALGOS[a], sizes=(1024, 1 << 16))
+               for a in ("naive_twoshot", "ring_sendrecv", "rhd_sendrecv", "pipelined_twoshot"))
+
+
+def test_verify_correctness_rank_fill():
+    assert all(run_ranks(_verify_worker, 2, backend="gloo", timeout=120))
+
+
+def test_world8_ring_and_rhd():
+    res = run_ranks(_worker, 8, backend="gloo",
+                    args=(["ring_sendrecv", "rhd_sendrecv", "naive_twoshot"], ["1KB", "1MB"], ["float32"], None),
+                    timeout=300)
+    bad = [r for rr in res for r in rr if not r[3]]
+    assert not bad, bad
