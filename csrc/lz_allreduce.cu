@@ -542,12 +542,12 @@ inline int clamp_int(long long v, int lo, int hi) {
 }  // namespace
 
 // Flag-area layout inside the heap (offsets from the heap base):
-//   [0, 16K)       barrier flags [LZ_MAX_BLOCKS][LZ_MAX_RANKS]
-//   [16K, 18K)     ring ready flags [LZ_MAX_BLOCKS]
-//   [18K, 20K)     ring credit flags [LZ_MAX_BLOCKS]
-//   [64K, 1M)      other protocols (weight transfer, compressed collectives)
-static constexpr size_t kRingReadyOff = 16384;
-static constexpr size_t kRingCreditOff = 18432;
+//   [0, 32K)       barrier flags [LZ_MAX_BLOCKS][LZ_MAX_RANKS]
+//   [32K, 36K)     ring ready flags [LZ_MAX_BLOCKS]
+//   [36K, 40K)     ring credit flags [LZ_MAX_BLOCKS]
+//   [64K, 1M)      other protocols (weight transfer)
+static constexpr size_t kRingReadyOff = 32768;
+static constexpr size_t kRingCreditOff = 36864;
 
 static int init_comm_state(LzComm* c, int dev, size_t oneshot_bytes, size_t stage_bytes,
                            double timeout_s) {
@@ -920,7 +920,7 @@ extern "C" int lz_emu_create(int R, size_t heap_bytes, size_t oneshot_bytes, siz
     if (rc) return rc;
   }
   LZ_CUDA_TRY(cudaMalloc(&e->d_comms, sizeof(LzDevComm) * LZ_MAX_RANKS));
-  LZ_CUDA_TRY(cudaMalloc(&e->d_params, sizeof(ArParams) * LZ_MAX_RANKS));
+  LZ_CUDA_TRY(cudaMalloc(&e->d_params, 4096));  // also used by other emulated kernels
   LzDevComm hc[LZ_MAX_RANKS];
   for (int r = 0; r < R; ++r) hc[r] = e->comms[r].dev;
   LZ_CUDA_TRY(cudaMemcpy(e->d_comms, hc, sizeof(LzDevComm) * R, cudaMemcpyHostToDevice));
@@ -949,6 +949,8 @@ extern "C" int lz_emu_status(LzEmu* e, int r) {
 }
 LzComm* lz_emu_comm(LzEmu* e, int r) { return &e->comms[r]; }
 LzDevComm* lz_emu_dev_comms(LzEmu* e) { return e->d_comms; }
+int lz_emu_world(LzEmu* e) { return e->R; }
+void* lz_emu_param_buffer(LzEmu* e) { return e->d_params; }
 
 extern "C" int lz_emu_allreduce(LzEmu* e, const void* const* ins, void* const* outs, size_t count,
                                 int dtype, int algo, int nblocks, int nthreads, cudaStream_t s) {

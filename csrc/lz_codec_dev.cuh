@@ -286,8 +286,7 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
     if (act) {
       uint4 v[S::IN_VECS];
 #pragma unroll
-      for (int q = 0; q < S::IN_VECS; ++q)
-        v[q] = *reinterpret_cast<const uint4*>(in + (size_t)u * 16 * ES + 16 * q);
+      for (int q = 0; q < S::IN_VECS; ++q) v[q] = ld_cg_v4(in + (size_t)u * 16 * ES + 16 * q);
       uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 1];
       S::split(v, sy, rw);
       *reinterpret_cast<uint4*>(&sm.syms[u * 16]) = *reinterpret_cast<const uint4*>(sy);
@@ -420,16 +419,13 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
 }
 
 // ---------------------------------------------------------------------------
-// Decode one TG record at `src` (n elements expected) into `out`.
-// Returns true on success (uniform over the CTA); on a corrupt record nothing
-// beyond `out[0, n)` is written and false is returned.
+// Decode the symbol plane of the TG record at `src` (n elements expected)
+// into sm.syms. Returns true on success (uniform over the CTA); the raw plane
+// starts at src + sizeof(TgHeader). A corrupt record returns false.
 // ---------------------------------------------------------------------------
 template <int DT>
-LZ_DEV bool decode_tg(const char* __restrict__ src, uint32_t cap, uint32_t n, char* __restrict__ out,
-                      DecSmem& sm) {
-  using S = Split16<DT>;
+LZ_DEV bool decode_tg_syms(const char* __restrict__ src, uint32_t cap, uint32_t n, DecSmem& sm) {
   constexpr int RB = DT == DT_F32 ? 3 : (DT == DT_U8 ? 0 : 1);
-  constexpr int ES = DT == DT_F32 ? 4 : (DT == DT_U8 ? 1 : 2);
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     TgHeader h;
@@ -563,7 +559,17 @@ LZ_DEV bool decode_tg(const char* __restrict__ src, uint32_t cap, uint32_t n, ch
     if (!sm.ok) return false;
   }
   __syncthreads();
-  // merge symbols with the raw plane
+  return true;
+}
+
+// Merge decoded symbols with the raw plane and store the elements.
+template <int DT>
+LZ_DEV void merge_store(const char* __restrict__ raw, const DecSmem& sm, uint32_t n,
+                        char* __restrict__ out) {
+  using S = Split16<DT>;
+  constexpr int RB = DT == DT_F32 ? 3 : (DT == DT_U8 ? 0 : 1);
+  constexpr int ES = DT == DT_F32 ? 4 : (DT == DT_U8 ? 1 : 2);
+  const uint32_t tid = threadIdx.x;
   const uint32_t units = n / 16;
   for (uint32_t u = tid; u < units; u += blockDim.x) {
     uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 16];
@@ -574,16 +580,77 @@ LZ_DEV bool decode_tg(const char* __restrict__ src, uint32_t cap, uint32_t n, ch
     uint4 v[S::IN_VECS];
     S::merge(reinterpret_cast<const uint8_t*>(&sv), rw, v);
 #pragma unroll
-    for (int q = 0; q < S::IN_VECS; ++q)
-      st_v4(out + (size_t)u * 16 * ES + 16 * q, v[q]);
+    for (int q = 0; q < S::IN_VECS; ++q) st_v4(out + (size_t)u * 16 * ES + 16 * q, v[q]);
   }
   if (tid < n - units * 16) {
     const uint32_t i = units * 16 + tid;
     uint8_t r1[4] = {0, 0, 0, 0};
-    for (int q = 0; q < RB; ++q) r1[q] = (uint8_t)raw[(size_t)i * RB + q];
+    for (int q = 0; q < RB; ++q) r1[q] = ld_cg_u8(raw + (size_t)i * RB + q);
     merge1<DT>(out, i, sm.syms[i], r1);
   }
   __syncthreads();
+}
+
+// Element value of decoded symbol + raw bits as fp32 (float dtypes only).
+template <int DT>
+LZ_DEV float elem_to_f32(uint8_t sym, const uint8_t* raw) {
+  if (DT == DT_BF16) return __uint_as_float((uint32_t)merge_bf16(sym, raw[0]) << 16);
+  if (DT == DT_F16) return __half2float(__ushort_as_half(merge_f16(sym, raw[0])));
+  const uint32_t r = raw[0] | ((uint32_t)raw[1] << 8) | ((uint32_t)raw[2] << 16);
+  return __uint_as_float(merge_f32(sym, r));
+}
+
+// acc[i] (fp32, global scratch) = or += value of element i. Same thread owns
+// the same 16 elements in every call, so no synchronisation between calls.
+template <int DT>
+LZ_DEV void merge_accumulate(const char* __restrict__ raw, const DecSmem& sm, uint32_t n,
+                             float* __restrict__ acc, bool first) {
+  using S = Split16<DT>;
+  constexpr int RB = DT == DT_F32 ? 3 : 1;
+  const uint32_t tid = threadIdx.x;
+  const uint32_t units = (n + 15) / 16;
+  for (uint32_t u = tid; u < units; u += blockDim.x) {
+    uint8_t rw[S::RAW_BYTES];
+    uint8_t sy[16];
+    if ((u + 1) * 16 <= n) {
+#pragma unroll
+      for (int q = 0; q < S::RAW_BYTES / 16; ++q)
+        reinterpret_cast<uint4*>(rw)[q] = ld_cg_v4(raw + (size_t)u * S::RAW_BYTES + 16 * q);
+      *reinterpret_cast<uint4*>(sy) = *reinterpret_cast<const uint4*>(&sm.syms[u * 16]);
+    } else {
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t i = u * 16 + k;
+        sy[k] = i < n ? sm.syms[i] : 0;
+        for (int q = 0; q < RB; ++q) rw[k * RB + q] = i < n ? ld_cg_u8(raw + (size_t)i * RB + q) : 0;
+      }
+    }
+    float4* a4 = reinterpret_cast<float4*>(acc + (size_t)u * 16);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float4 v;
+      v.x = elem_to_f32<DT>(sy[4 * q + 0], rw + (4 * q + 0) * RB);
+      v.y = elem_to_f32<DT>(sy[4 * q + 1], rw + (4 * q + 1) * RB);
+      v.z = elem_to_f32<DT>(sy[4 * q + 2], rw + (4 * q + 2) * RB);
+      v.w = elem_to_f32<DT>(sy[4 * q + 3], rw + (4 * q + 3) * RB);
+      if (!first) {
+        const float4 o = a4[q];
+        v.x = o.x + v.x;
+        v.y = o.y + v.y;
+        v.z = o.z + v.z;
+        v.w = o.w + v.w;
+      }
+      a4[q] = v;
+    }
+  }
+}
+
+// Decode one TG record at `src` (n elements expected) into `out`.
+// Returns true on success (uniform over the CTA).
+template <int DT>
+LZ_DEV bool decode_tg(const char* __restrict__ src, uint32_t cap, uint32_t n, char* __restrict__ out,
+                      DecSmem& sm) {
+  if (!decode_tg_syms<DT>(src, cap, n, sm)) return false;
+  merge_store<DT>(src + sizeof(TgHeader), sm, n, out);
   return true;
 }
 

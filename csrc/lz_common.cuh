@@ -63,6 +63,16 @@ LZ_DEV uint4 ld_nc_v4(const void* p) {  // read-only for the kernel's lifetime
                : "l"(p));
   return v;
 }
+LZ_DEV uint8_t ld_cg_u8(const void* p) {
+  unsigned short v;
+  asm volatile("ld.global.cg.u8 %0, [%1];" : "=h"(v) : "l"(p));
+  return (uint8_t)v;
+}
+LZ_DEV uint32_t ld_cg_u32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
 LZ_DEV void st_v4(void* p, uint4 v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w)

@@ -1,0 +1,333 @@
+// Lossless compressed allreduce, fused with the NVLink transfer.
+//
+// One persistent launch per call, three phases separated by per-CTA
+// all-pairs flag barriers (bounded waits):
+//   1. RS encode+push: every table group (TG) of every peer's slice is
+//      split + rANS-encoded by this GPU and the record is written straight
+//      into the peer's receive slot (peer stores over NVLink): only the
+//      compressed bytes cross the link, no staging copy, no size exchange.
+//   2. decode+reduce: the owner decodes the W-1 incoming records of each of
+//      its TGs and accumulates them with its own input in fp32 in rank order
+//      0..W-1 (bit-identical to an fp32 sequential reference), rounds once,
+//      stores its output slice, re-encodes the reduced TG once and publishes
+//      the record to every peer (NVLS multimem.st when a multicast object
+//      exists: one store reaches all GPUs; else peer stores).
+//   3. AG decode: every rank decodes the W-1 published records of the other
+//      slices straight into its output.
+// Records are never truncated: a TG that does not compress is stored RAW.
+//
+// Reference behaviour being re-designed: the compressed two-shot all-to-all
+// ("LZip two-shot", single_node_nccl_allreduce_benchmark/compressed_twoshot_allreduce.py:126-247),
+// which compresses with dietgpu, sends a fixed 0.65-ratio prefix with NCCL
+// (silently truncating streams that do not fit, :177-178) and decompresses in
+// separate launches; and the compressed P2P hybrid
+// (single_node_nccl_allreduce_benchmark/compressed_p2p_allreduce.py:54-188).
+#include "lz_codec_dev.cuh"
+#include "lz_internal.h"
+
+using namespace lzc;
+using namespace lzg;
+
+namespace {
+
+struct CzParams {
+  const char* in;
+  char* out;
+  uint64_t n;          // elements
+  uint64_t slice;      // elements per slice (multiple of 16); slice p = [p*slice, ...)
+  uint32_t ntg_max;    // TGs per slice (max)
+  uint32_t cap;        // TG record capacity
+  size_t rs_off;       // heap offset: RS slots [src][tg]
+  size_t ag_off;       // heap offset: AG slots [owner][tg]
+  float* acc;          // local fp32 scratch, TG_ELEMS per CTA
+  int use_mc;          // publish AG records with multimem.st
+};
+
+union CzSmem {
+  EncSmem enc;
+  DecSmem dec;
+};
+
+LZ_DEV uint64_t slice_begin(const CzParams& p, int s) {
+  const uint64_t b = (uint64_t)s * p.slice;
+  return b < p.n ? b : p.n;
+}
+LZ_DEV uint64_t slice_len(const CzParams& p, int s) {
+  const uint64_t b = slice_begin(p, s), e = slice_begin(p, s + 1);
+  return e - b;
+}
+LZ_DEV uint32_t ntg_of(const CzParams& p, int s) { return (uint32_t)num_tgs(slice_len(p, s)); }
+
+template <int DT>
+LZ_DEV void accumulate_plain(const char* __restrict__ in, uint32_t n, float* __restrict__ acc,
+                             bool first) {
+  constexpr int ES = DT == DT_F32 ? 4 : 2;
+  for (uint32_t i0 = threadIdx.x * 16; i0 < n; i0 += blockDim.x * 16) {
+    float v[16];
+    if (i0 + 16 <= n) {
+      uint4 raw[ES * 16 / 16];
+#pragma unroll
+      for (int q = 0; q < ES; ++q) raw[q] = ld_cg_v4(in + (size_t)i0 * ES + 16 * q);
+      if (DT == DT_F32) {
+        const float* f = reinterpret_cast<const float*>(raw);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = f[k];
+      } else if (DT == DT_BF16) {
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(raw);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = __bfloat162float(h[k]);
+      } else {
+        const __half* h = reinterpret_cast<const __half*>(raw);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = __half2float(h[k]);
+      }
+    } else {
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t i = i0 + k;
+        float x = 0.f;
+        if (i < n) {
+          if (DT == DT_F32) x = reinterpret_cast<const float*>(in)[i];
+          else if (DT == DT_BF16) x = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(in)[i]);
+          else x = __half2float(reinterpret_cast<const __half*>(in)[i]);
+        }
+        v[k] = x;
+      }
+    }
+    float4* a4 = reinterpret_cast<float4*>(acc + i0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float4 o = first ? make_float4(0.f, 0.f, 0.f, 0.f) : a4[q];
+      o.x = first ? v[4 * q] : o.x + v[4 * q];
+      o.y = first ? v[4 * q + 1] : o.y + v[4 * q + 1];
+      o.z = first ? v[4 * q + 2] : o.z + v[4 * q + 2];
+      o.w = first ? v[4 * q + 3] : o.w + v[4 * q + 3];
+      a4[q] = o;
+    }
+  }
+}
+
+template <int DT>
+LZ_DEV void store_rounded(const float* __restrict__ acc, uint32_t n, char* __restrict__ out) {
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float a = acc[i];
+    if (DT == DT_F32) reinterpret_cast<float*>(out)[i] = a;
+    else if (DT == DT_BF16) reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(a);
+    else reinterpret_cast<__half*>(out)[i] = __float2half_rn(a);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzParams& p) {
+  extern __shared__ __align__(16) char smem_raw[];
+  CzSmem& sm = *reinterpret_cast<CzSmem*>(smem_raw);
+  constexpr int ES = DT == DT_F32 ? 4 : 2;
+  const unsigned long long epoch = epoch_read(c);
+  const int W = c.world, me = c.rank, G = gridDim.x, b = blockIdx.x;
+  auto rs_slot = [&](int rank_heap, int src, uint32_t t) {
+    return c.heap[rank_heap] + p.rs_off + ((size_t)src * p.ntg_max + t) * p.cap;
+  };
+  auto ag_slot = [&](char* base, int owner, uint32_t t) {
+    return base + p.ag_off + ((size_t)owner * p.ntg_max + t) * p.cap;
+  };
+
+  // 1. encode my input's TGs of every peer's slice into that peer's RS slots
+  for (int k = 1; k < W; ++k) {
+    const int dst = (me + k) % W;
+    const uint64_t s0 = slice_begin(p, dst), sl = slice_len(p, dst);
+    const uint32_t nt = ntg_of(p, dst);
+    for (uint32_t t = b; t < nt; t += G) {
+      const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
+      encode_tg<DT>(p.in + (s0 + (uint64_t)t * TG_ELEMS) * ES, tn, rs_slot(dst, me, t), sm.enc);
+    }
+  }
+  if (!block_barrier(c, epoch, 1)) return;
+
+  // 2. decode + reduce (rank order, fp32) + store + re-encode + publish
+  {
+    const uint64_t s0 = slice_begin(p, me), sl = slice_len(p, me);
+    const uint32_t nt = ntg_of(p, me);
+    float* acc = p.acc + (size_t)b * TG_ELEMS;
+    __shared__ int s_bad;
+    for (uint32_t t = b; t < nt; t += G) {
+      const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
+      const uint64_t e0 = s0 + (uint64_t)t * TG_ELEMS;
+      for (int s = 0; s < W; ++s) {
+        if (s == me) {
+          accumulate_plain<DT>(p.in + e0 * ES, tn, acc, s == 0);
+        } else {
+          const char* rec = rs_slot(me, s, t);
+          if (!decode_tg_syms<DT>(rec, p.cap, tn, sm.dec)) {
+            if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 2, s);
+            return;
+          }
+          merge_accumulate<DT>(rec + sizeof(TgHeader), sm.dec, tn, acc, s == 0);
+        }
+        __syncthreads();
+      }
+      store_rounded<DT>(acc, tn, p.out + e0 * ES);
+      __syncthreads();
+      char* mine = ag_slot(c.heap[me], me, t);
+      const uint32_t bytes = encode_tg<DT>(p.out + e0 * ES, tn, mine, sm.enc);
+      const uint32_t padded = pad16(bytes);
+      if (p.use_mc) {
+        char* mc = ag_slot(c.heap_mc, me, t);
+        for (uint32_t o = threadIdx.x * 16; o < padded; o += blockDim.x * 16)
+          multimem_st_v4(mc + o, ld_cg_v4(mine + o));
+      } else {
+        for (int k = 1; k < W; ++k) {
+          char* dstp = ag_slot(c.heap[(me + k) % W], me, t);
+          for (uint32_t o = threadIdx.x * 16; o < padded; o += blockDim.x * 16)
+            st_v4(dstp + o, ld_cg_v4(mine + o));
+        }
+      }
+      __syncthreads();
+    }
+    (void)s_bad;
+  }
+  if (p.use_mc) {
+    if (!block_barrier_mc(c, epoch, 2)) return;
+  } else {
+    if (!block_barrier(c, epoch, 2)) return;
+  }
+
+  // 3. decode the other owners' reduced TGs into my output
+  for (int k = 1; k < W; ++k) {
+    const int own = (me + W - k) % W;
+    const uint64_t s0 = slice_begin(p, own), sl = slice_len(p, own);
+    const uint32_t nt = ntg_of(p, own);
+    for (uint32_t t = b; t < nt; t += G) {
+      const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
+      if (!decode_tg<DT>(ag_slot(c.heap[me], own, t), p.cap, tn, p.out + (s0 + (uint64_t)t * TG_ELEMS) * ES,
+                         sm.dec)) {
+        if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 3, own);
+        return;
+      }
+    }
+  }
+  epoch_advance(c);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(LZC_THREADS) cz_allreduce_kernel(LzDevComm c, CzParams p) {
+  cz_allreduce_body<DT>(c, p);
+}
+
+// Single-GPU emulation: block (x, y) is block x of rank y (cooperative launch).
+template <int DT>
+__global__ void __launch_bounds__(LZC_THREADS) cz_allreduce_emu_kernel(const LzDevComm* cs,
+                                                                       const CzParams* ps) {
+  cz_allreduce_body<DT>(cs[blockIdx.y], ps[blockIdx.y]);
+}
+
+template <int DT>
+void* cz_fn(bool emu) {
+  return emu ? reinterpret_cast<void*>(&cz_allreduce_emu_kernel<DT>)
+             : reinterpret_cast<void*>(&cz_allreduce_kernel<DT>);
+}
+
+void* cz_kernel_for(int dtype, bool emu) {
+  switch (dtype) {
+    case LZ_F32:
+      return cz_fn<DT_F32>(emu);
+    case LZ_F16:
+      return cz_fn<DT_F16>(emu);
+    default:
+      return cz_fn<DT_BF16>(emu);
+  }
+}
+
+}  // namespace
+
+// Bytes of the compressed-allreduce staging region for n elements.
+extern "C" size_t lz_cz_stage_bytes(size_t n, int dtype, int world, int nblocks) {
+  const uint64_t slice = ((n + world - 1) / world + 15) / 16 * 16;
+  const uint64_t ntg = num_tgs(slice);
+  const uint64_t cap = tg_capacity(dtype);
+  return 2 * (size_t)world * ntg * cap + (size_t)nblocks * TG_ELEMS * 4 + 256;
+}
+
+extern "C" int lz_cz_default_blocks(LzComm* c) { return c->sm_count * 3; }
+
+static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dtype, int G,
+                   int use_multicast, CzParams* out_p) {
+  const int W = c->dev.world;
+  if (dtype != LZ_F32 && dtype != LZ_F16 && dtype != LZ_BF16) {
+    lz_set_error("compressed allreduce: dtype %d not supported (float types only)", dtype);
+    return LZE_ARG;
+  }
+  if ((uintptr_t)in % 16 || (uintptr_t)out % 16) {
+    lz_set_error("compressed allreduce needs 16-byte aligned buffers");
+    return LZE_ARG;
+  }
+  CzParams p;
+  memset(&p, 0, sizeof(p));
+  p.in = static_cast<const char*>(in);
+  p.out = static_cast<char*>(out);
+  p.n = n;
+  p.slice = ((n + W - 1) / W + 15) / 16 * 16;
+  p.ntg_max = (uint32_t)num_tgs(p.slice);
+  p.cap = tg_capacity(dtype);
+  const size_t need = lz_cz_stage_bytes(n, dtype, W, G);
+  if (need > c->stage_bytes) {
+    lz_set_error("compressed allreduce: stage needs %zu bytes, communicator has %zu (raise stage_bytes)",
+                 need, c->stage_bytes);
+    return LZE_ARG;
+  }
+  p.rs_off = c->stage_off;
+  p.ag_off = c->stage_off + (size_t)W * p.ntg_max * p.cap;
+  p.acc = reinterpret_cast<float*>(c->dev.heap[c->dev.rank] + p.ag_off + (size_t)W * p.ntg_max * p.cap);
+  p.use_mc = (use_multicast && c->dev.heap_mc) ? 1 : 0;
+  *out_p = p;
+  return LZE_OK;
+}
+
+extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, size_t n, int dtype,
+                                       int nblocks, int use_multicast, cudaStream_t s) {
+  const int W = c->dev.world;
+  const size_t es = dtype == LZ_F32 ? 4 : 2;
+  if (W == 1) {
+    if (in != out) LZ_CUDA_TRY(cudaMemcpyAsync(out, in, n * es, cudaMemcpyDeviceToDevice, s));
+    return LZE_OK;
+  }
+  int G = nblocks > 0 ? nblocks : lz_cz_default_blocks(c);
+  if (G > LZ_MAX_BLOCKS) G = LZ_MAX_BLOCKS;
+  CzParams p;
+  int rc = cz_plan(c, in, out, n, dtype, G, use_multicast, &p);
+  if (rc) return rc;
+  void* fn = cz_kernel_for(dtype, false);
+  const size_t smem = sizeof(CzSmem);
+  LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  void* args[] = {&c->dev, &p};
+  LZ_CUDA_TRY(cudaLaunchKernel(fn, dim3(G), dim3(LZC_THREADS), args, smem, s));
+  return LZE_OK;
+}
+
+// Single-GPU emulation of the compressed allreduce over the R emulated ranks.
+extern "C" int lz_emu_compressed_allreduce(LzEmu* e, const void* const* ins, void* const* outs,
+                                           size_t n, int dtype, int nblocks, cudaStream_t s) {
+  const int R = lz_emu_world(e);
+  void* fn = cz_kernel_for(dtype, true);
+  const size_t smem = sizeof(CzSmem);
+  LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  LZ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, LZC_THREADS, smem));
+  const int cap = per_sm * lz_emu_comm(e, 0)->sm_count;
+  int G = nblocks > 0 ? nblocks : cap / R;
+  if (G * R > cap || G < 1) {
+    lz_set_error("emulated compressed allreduce: %d x %d blocks exceed co-residency %d", G, R, cap);
+    return LZE_ARG;
+  }
+  CzParams hp[LZ_MAX_RANKS];
+  for (int r = 0; r < R; ++r) {
+    int rc = cz_plan(lz_emu_comm(e, r), ins[r], outs[r], n, dtype, G, 0, &hp[r]);
+    if (rc) return rc;
+  }
+  static_assert(sizeof(CzParams) * LZ_MAX_RANKS <= 4096, "param buffer");
+  void* dparams = lz_emu_param_buffer(e);
+  LZ_CUDA_TRY(cudaMemcpyAsync(dparams, hp, sizeof(CzParams) * R, cudaMemcpyHostToDevice, s));
+  LzDevComm* dcomms = lz_emu_dev_comms(e);
+  void* args[] = {&dcomms, &dparams};
+  LZ_CUDA_TRY(cudaLaunchCooperativeKernel(fn, dim3(G, R), dim3(LZC_THREADS), args, smem, s));
+  LZ_CUDA_TRY(cudaStreamSynchronize(s));
+  return LZE_OK;
+}

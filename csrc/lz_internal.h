@@ -42,3 +42,10 @@ struct LzComm {
 // Returns the heap offset of [p, p+bytes) when it lies in this rank's heap, or
 // (size_t)-1.
 size_t lz_comm_heap_offset(const LzComm* c, const void* p, size_t bytes);
+
+// Single-GPU emulation internals shared between translation units.
+typedef struct LzEmu LzEmu;
+LzComm* lz_emu_comm(LzEmu* e, int r);
+LzDevComm* lz_emu_dev_comms(LzEmu* e);
+int lz_emu_world(LzEmu* e);
+void* lz_emu_param_buffer(LzEmu* e);  // 4 KB device buffer for per-rank params

@@ -4,7 +4,7 @@
 #include <stdint.h>
 
 #define LZ_MAX_RANKS 8
-#define LZ_MAX_BLOCKS 256
+#define LZ_MAX_BLOCKS 512
 
 // Status word codes (host mirror in lz_api.h).
 #define LZ_OK 0

@@ -62,6 +62,17 @@ class EmulatedWorld:
                                         s.cuda_stream)
         _native.check(rc, f"emulated allreduce[{algo}]")
 
+    def compressed_allreduce(self, ins, outs, nblocks: int = 0):
+        from . import compressed  # noqa: F401  (declares the native signature)
+
+        R = self.world
+        arr_in = (C.c_void_p * R)(*[t.data_ptr() for t in ins])
+        arr_out = (C.c_void_p * R)(*[t.data_ptr() for t in outs])
+        rc = self._lib.lz_emu_compressed_allreduce(self._emu, arr_in, arr_out, ins[0].numel(),
+                                                   lz_dtype(ins[0].dtype), nblocks,
+                                                   torch.cuda.current_stream().cuda_stream)
+        _native.check(rc, "emulated compressed allreduce")
+
     def status(self, r: int) -> int:
         return self._lib.lz_emu_status(self._emu, r)
 

@@ -35,7 +35,13 @@ def _worker(rank, world, cases):
         for x in xs[1:]:
             ref_acc += x.float()
         ref = ref_acc.to(dtype)
-        if sym:
+        if algo.startswith("compressed"):
+            from results_b200.parallel.compressed import compressed_allreduce
+
+            res = torch.empty_like(xs[rank])
+            for _ in range(3):
+                compressed_allreduce(xs[rank], res, comm=comm, multicast=(algo == "compressed_mc"))
+        elif sym:
             comm.reset_alloc()
             buf = comm.empty(n, dtype)
             for _ in range(3):
@@ -72,6 +78,9 @@ CASES = [
     ("nvls", "float32", 1 << 20, False, False),
     ("nvls", "bfloat16", (1 << 20) + 64, False, False),
     ("nvls_oneshot", "bfloat16", 1 << 14, False, False),
+    ("compressed", "bfloat16", (1 << 20) + 48, False, True),
+    ("compressed_mc", "bfloat16", 1 << 21, False, True),
+    ("compressed", "float32", 300_000, False, True),
 ]
 
 

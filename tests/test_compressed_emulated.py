@@ -1,0 +1,66 @@
+"""Fused compressed allreduce kernel on one GPU with R emulated ranks (one
+cooperative launch): bit-identical to the fp32 rank-order reference."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def worlds():
+    from results_b200.parallel.emulate import EmulatedWorld
+
+    ws = {R: EmulatedWorld(R, heap_bytes=(160 << 20), stage_bytes=(96 << 20)) for R in (2, 4)}
+    yield ws
+    for w in ws.values():
+        w.close()
+
+
+def _inputs(R, n, dtype, seed, kind="grad"):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    xs = []
+    for r in range(R):
+        if kind == "grad":
+            x = torch.randn(n, device="cuda", generator=g) * 1e-3
+        else:  # activation-like with 1% outliers x50
+            x = torch.randn(n, device="cuda", generator=g)
+            m = torch.rand(n, device="cuda", generator=g) < 0.01
+            x = torch.where(m, x * 50, x)
+        xs.append(x.to(dtype))
+    return xs
+
+
+@pytest.mark.parametrize("R", [2, 4])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("n", [16, 1000, 32768 * 3 + 48, 400_000])
+def test_compressed_allreduce_bitexact(worlds, R, dtype, n):
+    w = worlds[R]
+    xs = _inputs(R, n, dtype, seed=n + R)
+    outs = [torch.empty_like(x) for x in xs]
+    for _ in range(2):
+        w.compressed_allreduce(xs, outs, nblocks=8)
+    torch.cuda.synchronize()
+    acc = xs[0].float().clone()
+    for x in xs[1:]:
+        acc += x.float()
+    ref = acc.to(dtype)
+    for r in range(R):
+        assert w.status(r) == 0
+        assert torch.equal(outs[r].view(torch.uint8), ref.view(torch.uint8)), f"rank {r}"
+
+
+def test_compressed_inplace_activation_like(worlds):
+    R = 4
+    w = worlds[R]
+    n = 300_000
+    bufs = w.empty(n, torch.bfloat16)
+    xs = _inputs(R, n, torch.bfloat16, seed=5, kind="act")
+    for r in range(R):
+        bufs[r].copy_(xs[r])
+    w.compressed_allreduce(bufs, bufs, nblocks=16)
+    torch.cuda.synchronize()
+    acc = xs[0].float().clone()
+    for x in xs[1:]:
+        acc += x.float()
+    for r in range(R):
+        assert torch.equal(bufs[r], acc.to(torch.bfloat16))
