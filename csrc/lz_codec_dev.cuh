@@ -33,6 +33,8 @@ struct DecSmem {
   uint32_t dtab[PROB_SCALE];
   uint8_t syms[TG_ELEMS];
   uint8_t sec[TG_ELEMS];  // staged ANS symbol section (table, sizes, sub-streams)
+  uint32_t cum[257];      // cumulative frequencies of the table entries
+  uint32_t ent[256];      // table entries (sym << 16 | freq)
   TgHeader h;
   int ok;
 };
@@ -460,8 +462,8 @@ LZ_DEV bool decode_tg_syms(const char* __restrict__ src, uint32_t cap, uint32_t 
     __syncthreads();
     symsec = reinterpret_cast<const char*>(sm.sec);
     // decode table: slot -> entry, by binary search over the cumulative table
-    __shared__ uint32_t s_cum[257];
-    __shared__ uint32_t s_ent[256];
+    uint32_t* s_cum = sm.cum;
+    uint32_t* s_ent = sm.ent;
     if (warp == 0) {
       uint32_t e[8], f[8], lsum = 0;
 #pragma unroll

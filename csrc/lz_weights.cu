@@ -1,0 +1,270 @@
+// RL weight-update transfer: one sender (the trainer rank) to one or more
+// receivers (inference ranks), tensor by tensor, split+rANS encoded or raw.
+//
+// One persistent launch per bucket on every participating rank. The bucket is
+// a table of table-group (TG) descriptors; CTA b handles TGs b, b+G, ...
+// Receivers hold K slots per CTA; the sender waits for a slot's credit from
+// every receiver, encodes the TG (or takes it raw), publishes the record and
+// raises the receivers' ready flag; receivers decode into their destination
+// tensors and return the credit. When every rank receives, records and ready
+// flags go out with NVLS multimem.st (one store reaches all GPUs through the
+// switch); otherwise with peer stores. Flags carry (sequence << 32 | item+1)
+// with a sequence number per (sender, receiver) pair (or per sender for
+// all-rank broadcasts), so different calls never satisfy each other's waits.
+//
+// Reference behaviour being re-designed: the per-tensor NCCL broadcast of
+// back_up/update_weight_from_distributed.py:422-449 and the UCCL-P2P
+// split/encode sends whose logs and CSVs the reference keeps
+// (raw/bf16_split_sm16_split_encode_time_count.txt, csv/weight_update_rl_GLM4_9B.csv).
+#include "lz_codec_dev.cuh"
+#include "lz_internal.h"
+
+using namespace lzc;
+using namespace lzg;
+
+namespace {
+
+constexpr size_t kReadyP = 65536;    // [src][block] ready flags, point-to-point calls
+constexpr size_t kReadyB = 98304;    // [src][block] ready flags, all-rank broadcasts
+constexpr size_t kCreditP = 131072;  // [block][receiver] credits, point-to-point calls
+constexpr size_t kCreditB = 163840;  // [block][receiver] credits, all-rank broadcasts
+
+struct WxDesc {
+  char* ptr;        // sender: source bytes; receiver: destination bytes
+  uint32_t n;       // elements
+  uint8_t dtype;    // LZ dtype code
+  uint8_t encode;   // 1: split+rANS record, 0: raw bytes
+  uint16_t pad;
+};
+static_assert(sizeof(WxDesc) == 16, "descriptor layout");
+
+struct WxParams {
+  const WxDesc* descs;
+  uint32_t ntg;
+  int role;          // 0 sender, 1 receiver
+  int src;
+  uint32_t recv_mask;
+  int use_mc;
+  int kslots;
+  uint32_t cap;
+  size_t slots_off;
+  size_t ready_off;
+  size_t credit_off;
+  unsigned long long seq[LZ_MAX_RANKS];  // sender: per receiver; receiver: seq[0]
+};
+
+union WxSmem {
+  EncSmem enc;
+  DecSmem dec;
+};
+
+LZ_DEV int es_of(int dt) { return dt == LZ_F32 ? 4 : (dt == LZ_U8 ? 1 : 2); }
+
+// Byte copy of `bytes` from src to dst (16-B aligned both); the tail < 16 B is
+// assembled in a register and stored as one vector (dst capacity allows it).
+template <bool kMc>
+LZ_DEV void push_bytes(char* dst, const char* src, uint32_t bytes) {
+  const uint32_t full = bytes & ~15u;
+  for (uint32_t o = threadIdx.x * 16; o < full; o += blockDim.x * 16) {
+    const uint4 v = ld_cg_v4(src + o);
+    if (kMc) multimem_st_v4(dst + o, v);
+    else st_v4(dst + o, v);
+  }
+  if (threadIdx.x == 0 && full < bytes) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    uint8_t* vb = reinterpret_cast<uint8_t*>(&v);
+    for (uint32_t k = 0; k < bytes - full; ++k) vb[k] = ld_cg_u8(src + full + k);
+    if (kMc) multimem_st_v4(dst + full, v);
+    else st_v4(dst + full, v);
+  }
+}
+
+template <int DT>
+LZ_DEV uint32_t encode_any(const char* in, uint32_t n, char* dst, EncSmem& sm) {
+  return encode_tg<DT>(in, n, dst, sm);
+}
+
+LZ_DEV uint32_t encode_dispatch(int dt, const char* in, uint32_t n, char* dst, EncSmem& sm) {
+  switch (dt) {
+    case LZ_F32:
+      return encode_any<DT_F32>(in, n, dst, sm);
+    case LZ_F16:
+      return encode_any<DT_F16>(in, n, dst, sm);
+    case LZ_BF16:
+      return encode_any<DT_BF16>(in, n, dst, sm);
+    default:
+      return encode_any<DT_U8>(in, n, dst, sm);
+  }
+}
+
+LZ_DEV bool decode_dispatch(int dt, const char* rec, uint32_t cap, uint32_t n, char* out, DecSmem& sm) {
+  switch (dt) {
+    case LZ_F32:
+      return decode_tg<DT_F32>(rec, cap, n, out, sm);
+    case LZ_F16:
+      return decode_tg<DT_F16>(rec, cap, n, out, sm);
+    case LZ_BF16:
+      return decode_tg<DT_BF16>(rec, cap, n, out, sm);
+    default:
+      return decode_tg<DT_U8>(rec, cap, n, out, sm);
+  }
+}
+
+__device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
+  extern __shared__ __align__(16) char smem_raw[];
+  WxSmem& sm = *reinterpret_cast<WxSmem*>(smem_raw);
+  const int W = c.world, me = c.rank, G = gridDim.x, b = blockIdx.x;
+  const int K = p.kslots;
+  __shared__ int s_fail;
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  int nrecv = 0, only = -1;
+  for (int r = 0; r < W; ++r)
+    if ((p.recv_mask >> r) & 1u) {
+      ++nrecv;
+      only = r;
+    }
+
+  if (p.role == 0) {
+    // ---------------------------------------------------------------- sender
+    for (uint32_t i = 0; b + (uint64_t)i * G < p.ntg; ++i) {
+      const uint32_t t = b + i * G;
+      const uint32_t k = i % K;
+      const WxDesc d = p.descs[t];
+      const int t_r = threadIdx.x;
+      if (i >= (uint32_t)K && t_r < W && ((p.recv_mask >> t_r) & 1u)) {
+        const unsigned long long* cr = reinterpret_cast<const unsigned long long*>(
+            c.heap[me] + p.credit_off) + (size_t)b * LZ_MAX_RANKS + t_r;
+        if (!lz_wait_ge(c, cr, p.seq[t_r] | (unsigned long long)(i - K + 1), 5, t_r)) s_fail = 1;
+      }
+      __syncthreads();
+      if (s_fail) return;
+      const size_t slot_off = p.slots_off + ((size_t)b * K + k) * p.cap;
+      char* local = c.heap[me] + slot_off;
+      const int es = es_of(d.dtype);
+      if (d.encode) {
+        const bool direct = !p.use_mc && nrecv == 1;
+        char* dst = direct ? c.heap[only] + slot_off : local;
+        const uint32_t bytes = encode_dispatch(d.dtype, d.ptr, d.n, dst, sm.enc);
+        if (p.use_mc) {
+          push_bytes<true>(c.heap_mc + slot_off, local, pad16(bytes));
+        } else if (!direct) {
+          for (int r = 0; r < W; ++r)
+            if ((p.recv_mask >> r) & 1u) push_bytes<false>(c.heap[r] + slot_off, local, pad16(bytes));
+        }
+      } else {
+        const uint32_t bytes = d.n * (uint32_t)es;
+        if (p.use_mc) {
+          push_bytes<true>(c.heap_mc + slot_off, d.ptr, bytes);
+        } else {
+          for (int r = 0; r < W; ++r)
+            if ((p.recv_mask >> r) & 1u) push_bytes<false>(c.heap[r] + slot_off, d.ptr, bytes);
+        }
+      }
+      __syncthreads();
+      if (p.use_mc) {
+        if (threadIdx.x == 0) {
+          fence_sys();
+          unsigned long long* f = reinterpret_cast<unsigned long long*>(c.heap_mc + p.ready_off) +
+                                  (size_t)p.src * LZ_MAX_BLOCKS + b;
+          multimem_st_release_u64(f, p.seq[0] | (unsigned long long)(i + 1));
+        }
+      } else if (t_r < W && ((p.recv_mask >> t_r) & 1u)) {
+        fence_sys();
+        unsigned long long* f = reinterpret_cast<unsigned long long*>(c.heap[t_r] + p.ready_off) +
+                                (size_t)p.src * LZ_MAX_BLOCKS + b;
+        st_release_sys(f, p.seq[t_r] | (unsigned long long)(i + 1));
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- receiver
+    const unsigned long long* ready = reinterpret_cast<const unsigned long long*>(
+        c.heap[me] + p.ready_off) + (size_t)p.src * LZ_MAX_BLOCKS + b;
+    unsigned long long* credit = reinterpret_cast<unsigned long long*>(c.heap[p.src] + p.credit_off) +
+                                 (size_t)b * LZ_MAX_RANKS + me;
+    for (uint32_t i = 0; b + (uint64_t)i * G < p.ntg; ++i) {
+      const uint32_t t = b + i * G;
+      const uint32_t k = i % K;
+      const WxDesc d = p.descs[t];
+      if (threadIdx.x == 0 && !lz_wait_ge(c, ready, p.seq[0] | (unsigned long long)(i + 1), 6, p.src))
+        s_fail = 1;
+      __syncthreads();
+      if (s_fail) return;
+      if (threadIdx.x == 0 && p.use_mc) fence_proxy_alias();
+      __syncthreads();
+      const char* slot = c.heap[me] + p.slots_off + ((size_t)b * K + k) * p.cap;
+      if (d.encode) {
+        if (!decode_dispatch(d.dtype, slot, p.cap, d.n, d.ptr, sm.dec)) {
+          if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 7, p.src);
+          return;
+        }
+      } else {
+        const uint32_t bytes = d.n * (uint32_t)es_of(d.dtype);
+        const uint32_t full = bytes & ~15u;
+        for (uint32_t o = threadIdx.x * 16; o < full; o += blockDim.x * 16)
+          st_v4(d.ptr + o, ld_cg_v4(slot + o));
+        if (threadIdx.x < bytes - full) d.ptr[full + threadIdx.x] = (char)ld_cg_u8(slot + full + threadIdx.x);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        fence_sys();
+        st_release_sys(credit, p.seq[0] | (unsigned long long)(i + 1));
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(LZC_THREADS) wx_kernel(LzDevComm c, WxParams p) { wx_body(c, p); }
+
+}  // namespace
+
+extern "C" size_t lz_wx_slot_capacity(void) { return tg_capacity(LZ_F32); }
+extern "C" size_t lz_wx_tg_elems(void) { return TG_ELEMS; }
+
+// Stage bytes needed for `nblocks` CTAs with `kslots` slots each.
+extern "C" size_t lz_wx_stage_bytes(int nblocks, int kslots) {
+  return (size_t)nblocks * kslots * tg_capacity(LZ_F32);
+}
+
+// role 0 = sender (seq[r] per receiver r), 1 = receiver (seq[0]).
+// descs: device array of 16-byte descriptors (ptr, n, dtype, encode).
+extern "C" int lz_weight_transfer(LzComm* c, int role, int src, unsigned int recv_mask,
+                                  const void* descs, unsigned int ntg, int nblocks, int kslots,
+                                  int broadcast_all, const unsigned long long* seqs, cudaStream_t s) {
+  const int W = c->dev.world;
+  if (W == 1 || ntg == 0) return LZE_OK;
+  if (src < 0 || src >= W || (recv_mask >> src) & 1u || recv_mask == 0 ||
+      (recv_mask >> W) != 0u) {
+    lz_set_error("weight transfer: bad src %d / receiver mask 0x%x", src, recv_mask);
+    return LZE_ARG;
+  }
+  int G = nblocks > 0 ? nblocks : c->sm_count * 3;
+  if (G > LZ_MAX_BLOCKS) G = LZ_MAX_BLOCKS;
+  if (kslots < 2) kslots = 2;
+  WxParams p;
+  memset(&p, 0, sizeof(p));
+  p.descs = static_cast<const WxDesc*>(descs);
+  p.ntg = ntg;
+  p.role = role;
+  p.src = src;
+  p.recv_mask = recv_mask;
+  const bool all = broadcast_all && recv_mask == (((1u << W) - 1u) & ~(1u << src));
+  p.use_mc = (all && c->dev.heap_mc) ? 1 : 0;
+  p.kslots = kslots;
+  p.cap = tg_capacity(LZ_F32);
+  p.slots_off = c->stage_off;
+  if (lz_wx_stage_bytes(G, kslots) > c->stage_bytes) {
+    lz_set_error("weight transfer: %d blocks x %d slots need %zu stage bytes, have %zu", G, kslots,
+                 lz_wx_stage_bytes(G, kslots), c->stage_bytes);
+    return LZE_ARG;
+  }
+  p.ready_off = all ? kReadyB : kReadyP;
+  p.credit_off = all ? kCreditB : kCreditP;
+  for (int r = 0; r < LZ_MAX_RANKS; ++r) p.seq[r] = seqs[r] << 32;
+  const size_t smem = sizeof(WxSmem);
+  void* fn = reinterpret_cast<void*>(&wx_kernel);
+  LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  void* args[] = {&c->dev, &p};
+  LZ_CUDA_TRY(cudaLaunchKernel(fn, dim3(G), dim3(LZC_THREADS), args, smem, s));
+  return LZE_OK;
+}

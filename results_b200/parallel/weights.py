@@ -1,0 +1,281 @@
+"""RL weight-update transfer (trainer rank -> inference ranks).
+
+B200 design: one persistent kernel per bucket and rank (csrc/lz_weights.cu).
+Table groups of 32K elements are split + rANS encoded by the sender (or sent
+raw) into K slots per CTA on every receiver and decoded there straight into
+the destination tensors, chunk-pipelined with credits. When every other rank
+receives, records go out with NVLS multimem.st: the switch replicates one
+write to all receivers, so the sender's link carries each byte once.
+
+Public API::
+
+    wt = WeightTransfer(comm, mode="split_ans")      # or "raw"
+    wt.send(tensors, dsts=[1, 2])     # trainer
+    wt.recv(tensors, src=0)           # each receiver (destination tensors, same shapes)
+    wt.broadcast(tensors, src=0)      # all ranks; src sends, others receive
+    send_weights(state_dict, dst) / recv_weights(state_dict, src) / broadcast_weights(sd, src)
+
+Reference counterpart: UpdateWeightFromDistributed
+(back_up/update_weight_from_distributed.py:37-376): buckets by
+``update_weight_buffer_size`` (:259), per-tensor NCCL broadcast (:422-449),
+optional safetensors dump with a JSONL manifest (:93-160).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import os
+import time
+
+import torch
+import torch.distributed as dist
+
+from .. import _native, _native_sigs
+from ..utils.dtypes import lz_dtype
+
+_native_sigs.add_cuda({
+    "lz_wx_slot_capacity": (C.c_size_t,),
+    "lz_wx_tg_elems": (C.c_size_t,),
+    "lz_wx_stage_bytes": (C.c_size_t, C.c_int, C.c_int),
+    "lz_weight_transfer": (C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_uint, C.c_void_p, C.c_uint, C.c_int,
+                           C.c_int, C.c_int, C.POINTER(C.c_uint64), C.c_void_p),
+})
+
+TG = 32768
+MODES = ("raw", "split_ans")
+
+
+def _encode_flags(n_tensors: int, fraction: float):
+    """Evenly spread selection of round(fraction * n) tensors to encode."""
+    return [int((i + 1) * fraction) > int(i * fraction) for i in range(n_tensors)]
+
+
+def build_descriptors(tensors, encode, device) -> tuple[torch.Tensor, int]:
+    """16-byte descriptor per table group: (ptr, n | dtype << 32 | encode << 40)."""
+    rows_ptr, rows_meta = [], []
+    for t, enc in zip(tensors, encode):
+        if not t.is_contiguous():
+            raise ValueError("weight transfer needs contiguous tensors")
+        numel = t.numel()
+        if numel == 0:
+            continue
+        es = t.element_size()
+        base = t.data_ptr()
+        if base % 16:
+            raise ValueError("weight transfer needs 16-byte aligned tensors")
+        dt = lz_dtype(t.dtype) if t.dtype in (torch.float32, torch.float16, torch.bfloat16) else 3
+        ntg = (numel + TG - 1) // TG
+        idx = torch.arange(ntg, dtype=torch.int64)
+        rows_ptr.append(base + idx * (TG * es))
+        n = torch.clamp(numel - idx * TG, max=TG)
+        rows_meta.append(n | (dt << 32) | (int(bool(enc)) << 40))
+    if not rows_ptr:
+        return torch.empty(0, dtype=torch.int64, device=device), 0
+    d = torch.stack([torch.cat(rows_ptr), torch.cat(rows_meta)], dim=1).contiguous()
+    return d.pin_memory().to(device, non_blocking=True), d.shape[0]
+
+
+class WeightTransfer:
+    """Chunk-pipelined weight transfer engine on a :class:`Communicator`."""
+
+    def __init__(self, comm, mode: str = "split_ans", nblocks: int = 0, kslots: int = 0,
+                 chunk_bytes: int = 0, encode_fraction: float = 1.0):
+        if mode not in MODES:
+            raise ValueError(f"mode must be one of {MODES}")
+        self.comm = comm
+        self.mode = mode
+        self.encode_fraction = encode_fraction if mode == "split_ans" else 0.0
+        self.nblocks = nblocks or min(comm.sm_count * 3, 512)
+        cap_tg_bytes = TG * 2
+        if kslots:
+            self.kslots = kslots
+        elif chunk_bytes:
+            self.kslots = max(2, chunk_bytes // (self.nblocks * cap_tg_bytes))
+        else:
+            self.kslots = 4
+        lib = comm._lib
+        need = lib.lz_wx_stage_bytes(self.nblocks, self.kslots)
+        if need > comm.config.stage_bytes:
+            self.kslots = max(2, comm.config.stage_bytes // (self.nblocks * lib.lz_wx_slot_capacity()))
+        self.pair_seq: dict = {}
+        self.bcast_seq: dict = {}
+        self.bytes_sent = 0
+
+    @property
+    def window_bytes(self) -> int:
+        """Bytes in flight: blocks x slots x one table group of bf16."""
+        return self.nblocks * self.kslots * TG * 2
+
+    def _launch(self, role, src, mask, descs, ntg, all_, seqs):
+        arr = (C.c_uint64 * 8)(*seqs)
+        s = torch.cuda.current_stream(self.comm.device)
+        rc = self.comm._lib.lz_weight_transfer(self.comm.handle, role, src, mask, descs.data_ptr(), ntg,
+                                               self.nblocks, self.kslots, int(all_), arr, s.cuda_stream)
+        _native.check(rc, "weight transfer")
+
+    def _flags(self, tensors):
+        f = self.encode_fraction
+        return _encode_flags(len(tensors), f) if f > 0 else [False] * len(tensors)
+
+    def send(self, tensors, dsts, broadcast_all: bool = False) -> None:
+        tensors = list(tensors.values()) if isinstance(tensors, dict) else list(tensors)
+        dsts = [dsts] if isinstance(dsts, int) else list(dsts)
+        me = self.comm.rank
+        mask = 0
+        for d in dsts:
+            mask |= 1 << d
+        descs, ntg = build_descriptors(tensors, self._flags(tensors), f"cuda:{self.comm.device}")
+        seqs = [0] * 8
+        if broadcast_all:
+            s = self.bcast_seq.get(me, 0) + 1
+            self.bcast_seq[me] = s
+            seqs = [s] * 8
+        else:
+            for d in dsts:
+                s = self.pair_seq.get((me, d), 0) + 1
+                self.pair_seq[(me, d)] = s
+                seqs[d] = s
+        self.bytes_sent += sum(t.numel() * t.element_size() for t in tensors)
+        self._launch(0, me, mask, descs, ntg, broadcast_all, seqs)
+        self._keep = descs  # descriptors must outlive the launch
+
+    def recv(self, tensors, src: int, broadcast_all: bool = False) -> None:
+        tensors = list(tensors.values()) if isinstance(tensors, dict) else list(tensors)
+        me = self.comm.rank
+        descs, ntg = build_descriptors(tensors, self._flags(tensors), f"cuda:{self.comm.device}")
+        if broadcast_all:
+            s = self.bcast_seq.get(src, 0) + 1
+            self.bcast_seq[src] = s
+            mask = ((1 << self.comm.world) - 1) & ~(1 << src)
+        else:
+            s = self.pair_seq.get((src, me), 0) + 1
+            self.pair_seq[(src, me)] = s
+            mask = 1 << me
+        self._launch(1, src, mask, descs, ntg, broadcast_all, [s] * 8)
+        self._keep = descs
+
+    def broadcast(self, tensors, src: int) -> None:
+        """All ranks call; `src` sends its tensors, every other rank receives into its own."""
+        others = [r for r in range(self.comm.world) if r != src]
+        if self.comm.world == 1:
+            return
+        if self.comm.rank == src:
+            self.send(tensors, others, broadcast_all=True)
+        else:
+            self.recv(tensors, src, broadcast_all=True)
+
+
+# ---------------------------------------------------------------------- buckets
+def buckets(named, max_bytes: int):
+    """Group (name, tensor) pairs into buckets of at most `max_bytes` (one oversize tensor alone)."""
+    cur, size = [], 0
+    for name, t in named:
+        nb = t.numel() * t.element_size()
+        if cur and size + nb > max_bytes:
+            yield cur
+            cur, size = [], 0
+        cur.append((name, t))
+        size += nb
+    if cur:
+        yield cur
+
+
+def _engine(comm, mode, **kw):
+    from .allreduce import get_comm, init
+
+    comm = comm or get_comm() or init()
+    key = (id(comm), mode, tuple(sorted(kw.items())))
+    cache = _engine.__dict__.setdefault("cache", {})
+    if key not in cache:
+        cache[key] = WeightTransfer(comm, mode=mode, **kw)
+    return cache[key]
+
+
+def send_weights(state_dict, dst, comm=None, mode: str = "split_ans", bucket_bytes: int | None = None,
+                 dump_dir: str | None = None, weight_version: int = 0, **kw) -> None:
+    """Send a state_dict (name -> CUDA tensor) to rank(s) `dst`, bucket by bucket."""
+    eng = _engine(comm, mode, **kw)
+    bb = bucket_bytes or eng.comm.config.update_weight_buffer_bytes
+    for i, bucket in enumerate(buckets(list(state_dict.items()), bb)):
+        if dump_dir:
+            dump_tensors(bucket, dump_dir, weight_version, i, group_name=f"src{eng.comm.rank}")
+        eng.send([t for _, t in bucket], dst)
+
+
+def recv_weights(state_dict, src: int, comm=None, mode: str = "split_ans", bucket_bytes: int | None = None,
+                 **kw) -> dict:
+    """Receive into the destination tensors of `state_dict` (same names, shapes, order)."""
+    eng = _engine(comm, mode, **kw)
+    bb = bucket_bytes or eng.comm.config.update_weight_buffer_bytes
+    for bucket in buckets(list(state_dict.items()), bb):
+        eng.recv([t for _, t in bucket], src)
+    return state_dict
+
+
+def broadcast_weights(state_dict, src: int = 0, comm=None, mode: str = "split_ans",
+                      bucket_bytes: int | None = None, **kw) -> dict:
+    eng = _engine(comm, mode, **kw)
+    bb = bucket_bytes or eng.comm.config.update_weight_buffer_bytes
+    for bucket in buckets(list(state_dict.items()), bb):
+        eng.broadcast([t for _, t in bucket], src)
+    return state_dict
+
+
+def exchange_metadata(state_dict, src: int, group=None):
+    """Receivers learn (name, shape, dtype) of the sender's tensors (host control plane)."""
+    meta = [[(k, tuple(v.shape), str(v.dtype)) for k, v in state_dict.items()] if state_dict else None]
+    dist.broadcast_object_list(meta, src=src, group=group)
+    return meta[0]
+
+
+def allocate_like(meta, device) -> dict:
+    return {k: torch.empty(shape, dtype=getattr(torch, dt.replace("torch.", "")), device=device)
+            for k, shape, dt in meta}
+
+
+# ---------------------------------------------------------------------- dump / manifest
+def dump_tensors(named, dump_dir: str, weight_version: int, shard_idx: int, group_name: str = "") -> str:
+    """weight_version_XXXXXX/shard_XXXXXX.safetensors + appended manifest.jsonl
+    (same layout as back_up/update_weight_from_distributed.py:93-160)."""
+    step_dir = os.path.join(dump_dir, f"weight_version_{weight_version:06d}")
+    os.makedirs(step_dir, exist_ok=True)
+    cpu_state, meta = {}, []
+    for name, t in named:
+        tt = t.detach().contiguous().cpu()
+        cpu_state[name] = tt
+        meta.append({"name": name, "dtype": str(tt.dtype).replace("torch.", ""), "shape": list(tt.shape),
+                     "numel": tt.numel(), "nbytes": tt.numel() * tt.element_size()})
+    base = f"shard_{shard_idx:06d}"
+    try:
+        from safetensors.torch import save_file
+
+        path = os.path.join(step_dir, base + ".safetensors")
+        save_file(cpu_state, path)
+        fmt = "safetensors"
+    except Exception:
+        path = os.path.join(step_dir, base + ".pt")
+        torch.save(cpu_state, path)
+        fmt = "pt"
+    rec = {"time": time.time(), "weight_version": int(weight_version), "group_name": group_name,
+           "shard": os.path.basename(path), "num_tensors": len(cpu_state),
+           "total_nbytes": int(sum(m["nbytes"] for m in meta)), "tensors": meta, "format": fmt}
+    with open(os.path.join(step_dir, "manifest.jsonl"), "a", encoding="utf-8") as f:
+        f.write(json.dumps(rec) + "\n")
+    return path
+
+
+def load_dump(dump_dir: str, weight_version: int) -> dict:
+    """Read back every shard of a dumped weight version (bit-exact oracle for receivers)."""
+    step_dir = os.path.join(dump_dir, f"weight_version_{weight_version:06d}")
+    out = {}
+    with open(os.path.join(step_dir, "manifest.jsonl")) as f:
+        for line in f:
+            rec = json.loads(line)
+            p = os.path.join(step_dir, rec["shard"])
+            if rec["format"] == "safetensors":
+                from safetensors.torch import load_file
+
+                out.update(load_file(p))
+            else:
+                out.update(torch.load(p))
+    return out

@@ -1,0 +1,52 @@
+"""Host-side pieces of the weight-transfer engine (no GPU): encode-fraction
+selection, bucketing by byte budget, model shapes and the dump manifest."""
+import json
+import os
+
+import torch
+
+from results_b200.models import shapes
+from results_b200.parallel import weights
+
+
+def test_encode_fraction_selection():
+    for n in (1, 7, 10, 523):
+        for f in (0.0, 0.2, 0.4, 0.6, 0.8, 1.0):
+            flags = weights._encode_flags(n, f)
+            assert sum(flags) == int(n * f)
+
+
+def test_buckets_respect_budget():
+    named = [(f"t{i}", torch.empty(1000 * (i % 5 + 1), dtype=torch.bfloat16)) for i in range(40)]
+    out = list(weights.buckets(named, 6000))
+    assert sum(len(b) for b in out) == 40
+    for b in out:
+        size = sum(t.numel() * 2 for _, t in b)
+        assert size <= 6000 or len(b) == 1
+
+
+def test_glm4_shapes_match_reference_rows():
+    specs = {s.name: s for s in shapes.glm4_9b_specs()}
+    # per-tensor sizes of csv/weight_update_rl_GLM4_9B.csv: gate_up 214 MB, down 107 MB, o/q 32 MB
+    assert specs["model.layers.0.mlp.gate_up_proj.weight"].numel * 2 == 224_395_264
+    assert specs["model.layers.0.mlp.down_proj.weight"].numel * 2 == 112_197_632
+    assert specs["model.layers.0.self_attn.o_proj.weight"].numel * 2 == 33_554_432
+    assert abs(shapes.total_params(list(specs.values())) / 1e9 - 9.4) < 0.05
+
+
+def test_qwen_moe_shapes():
+    specs = shapes.qwen35_a3b_specs()
+    total = shapes.total_params(specs) / 1e9
+    assert 30 < total < 40
+    experts = [s for s in specs if "experts." in s.name]
+    assert all(s.numel * 2 >= 64 << 20 for s in experts)  # coalesced >= 64 MB chunks
+
+
+def test_dump_manifest_roundtrip(tmp_path):
+    named = [("a.weight", torch.randn(8, 4).to(torch.bfloat16)), ("b.bias", torch.randn(3))]
+    p = weights.dump_tensors(named, str(tmp_path), 12, 0, group_name="g")
+    assert os.path.exists(p)
+    rec = json.loads(open(os.path.join(tmp_path, "weight_version_000012", "manifest.jsonl")).readline())
+    assert rec["num_tensors"] == 2 and rec["tensors"][0]["shape"] == [8, 4]
+    back = weights.load_dump(str(tmp_path), 12)
+    assert torch.equal(back["a.weight"].view(torch.int16), named[0][1].view(torch.int16))
