@@ -97,8 +97,13 @@ class WeightTransfer:
         need = lib.lz_wx_stage_bytes(self.nblocks, self.kslots)
         if need > comm.config.stage_bytes:
             self.kslots = max(2, comm.config.stage_bytes // (self.nblocks * lib.lz_wx_slot_capacity()))
-        self.pair_seq: dict = {}
-        self.bcast_seq: dict = {}
+        # Flag sequence numbers must be monotonic per communicator (not per
+        # engine): every engine on `comm` shares the same flag words.
+        if not hasattr(comm, "_wx_pair_seq"):
+            comm._wx_pair_seq = {}
+            comm._wx_bcast_seq = {}
+        self.pair_seq: dict = comm._wx_pair_seq
+        self.bcast_seq: dict = comm._wx_bcast_seq
         self.bytes_sent = 0
 
     @property
