@@ -43,6 +43,14 @@ inline void split_elem(const uint8_t* data, int dt, uint32_t i, uint8_t* sym, ui
       raw[2] = (uint8_t)(r >> 16);
       break;
     }
+    case DT_E4M3P:
+    case DT_E5M2P: {
+      const uint8_t a = data[2 * (size_t)i], b = data[2 * (size_t)i + 1];
+      const uint16_t u = dt == DT_E4M3P ? pack_e4m3(a, b) : pack_e5m2(a, b);
+      *sym = sym_bf16(u);
+      raw[0] = raw_bf16(u);
+      break;
+    }
     default:
       *sym = data[i];
   }
@@ -64,6 +72,13 @@ inline void merge_elem(uint8_t* out, int dt, uint32_t i, uint8_t sym, const uint
       uint32_t r = raw[0] | ((uint32_t)raw[1] << 8) | ((uint32_t)raw[2] << 16);
       uint32_t u = merge_f32(sym, r);
       memcpy(out + 4 * (size_t)i, &u, 4);
+      break;
+    }
+    case DT_E4M3P:
+    case DT_E5M2P: {
+      const uint16_t u = merge_bf16(sym, raw[0]);
+      if (dt == DT_E4M3P) unpack_e4m3(u, out + 2 * (size_t)i, out + 2 * (size_t)i + 1);
+      else unpack_e5m2(u, out + 2 * (size_t)i, out + 2 * (size_t)i + 1);
       break;
     }
     default:
@@ -147,7 +162,7 @@ uint64_t lzc_max_stream_bytes(uint64_t n, int dt) { return max_stream_bytes(n, d
 // Encodes one TG of n (<= TG_ELEMS) elements into `out` (capacity
 // tg_capacity_n). Returns the record size.
 int64_t lzc_tg_encode(const void* data, uint32_t n, int dt, void* out_) {
-  if (n > TG_ELEMS) return -1;
+  if (n > TG_ELEMS || !valid_dtype(dt)) return -1;
   uint8_t* out = static_cast<uint8_t*>(out_);
   const uint8_t* in = static_cast<const uint8_t*>(data);
   const int rb = raw_bytes_per_elem(dt);
@@ -232,7 +247,7 @@ int lzc_tg_decode(const void* rec_, uint64_t rec_cap, void* out, uint32_t n, int
   if (rec_cap < sizeof(TgHeader)) return -2;
   TgHeader h;
   memcpy(&h, rec, sizeof(h));
-  if (h.magic != TG_MAGIC || h.version != VERSION || h.dtype != dt || h.n != n) return -3;
+  if (!valid_dtype(dt) || h.magic != TG_MAGIC || h.version != VERSION || h.dtype != dt || h.n != n) return -3;
   const int rb = raw_bytes_per_elem(dt);
   if (h.raw_bytes != pad16(n * (uint32_t)rb) || h.total > rec_cap ||
       h.total != sizeof(TgHeader) + h.raw_bytes + h.sym_bytes)
@@ -338,48 +353,18 @@ void lzc_histogram(const void* data, uint64_t n, int dt, uint64_t* counts) {
 }
 
 // ---- fp8 -------------------------------------------------------------------
-// e4m3 pair container (layout of back_up/fp8_e4m3fn_pack_benchmark.cu:21-31):
-// [15]=a.sign [14:11]=a.exp [10:7]=b.exp [6:4]=a.mant [3]=b.sign [2:0]=b.mant,
-// so bits 14..7 (the bf16 exponent byte) carry both exponents.
+// Pair containers (layouts in lz_codec_format.h).
 void lz_cpu_pack_e4m3(const uint8_t* in, uint16_t* out, uint64_t npairs) {
-  for (uint64_t i = 0; i < npairs; ++i) {
-    const uint8_t a = in[2 * i], b = in[2 * i + 1];
-    out[i] = (uint16_t)(((a & 0x80u) << 8) | ((a & 0x78u) << 8) | ((b & 0x78u) << 4) |
-                        ((a & 0x07u) << 4) | ((b & 0x80u) >> 4) | (b & 0x07u));
-  }
+  for (uint64_t i = 0; i < npairs; ++i) out[i] = pack_e4m3(in[2 * i], in[2 * i + 1]);
 }
-
 void lz_cpu_unpack_e4m3(const uint16_t* in, uint8_t* out, uint64_t npairs) {
-  for (uint64_t i = 0; i < npairs; ++i) {
-    const uint16_t w = in[i];
-    out[2 * i] = (uint8_t)(((w >> 8) & 0x80u) | ((w >> 8) & 0x78u) | ((w >> 4) & 0x07u));
-    out[2 * i + 1] = (uint8_t)(((w << 4) & 0x80u) | ((w >> 4) & 0x78u) | (w & 0x07u));
-  }
+  for (uint64_t i = 0; i < npairs; ++i) unpack_e4m3(in[i], out + 2 * i, out + 2 * i + 1);
 }
-
-// e5m2 pair container: two 5-bit exponents do not fit one byte, so the
-// container keeps the high 4 exponent bits of each value in bits 14..7 (the
-// symbol byte) and moves the remaining bits to the raw byte:
-// [15]=a.sign [14:11]=a.e[4:1] [10:7]=b.e[4:1] [6]=a.e[0] [5:4]=a.mant
-// [3]=b.sign [2]=b.e[0] [1:0]=b.mant
 void lz_cpu_pack_e5m2(const uint8_t* in, uint16_t* out, uint64_t npairs) {
-  for (uint64_t i = 0; i < npairs; ++i) {
-    const uint32_t a = in[2 * i], b = in[2 * i + 1];
-    const uint32_t ae = (a >> 2) & 0x1F, be = (b >> 2) & 0x1F;
-    out[i] = (uint16_t)(((a & 0x80u) << 8) | ((ae >> 1) << 11) | ((be >> 1) << 7) |
-                        ((ae & 1u) << 6) | ((a & 0x3u) << 4) | ((b & 0x80u) >> 4) |
-                        ((be & 1u) << 2) | (b & 0x3u));
-  }
+  for (uint64_t i = 0; i < npairs; ++i) out[i] = pack_e5m2(in[2 * i], in[2 * i + 1]);
 }
-
 void lz_cpu_unpack_e5m2(const uint16_t* in, uint8_t* out, uint64_t npairs) {
-  for (uint64_t i = 0; i < npairs; ++i) {
-    const uint32_t w = in[i];
-    const uint32_t ae = (((w >> 11) & 0xF) << 1) | ((w >> 6) & 1);
-    const uint32_t be = (((w >> 7) & 0xF) << 1) | ((w >> 2) & 1);
-    out[2 * i] = (uint8_t)(((w >> 8) & 0x80u) | (ae << 2) | ((w >> 4) & 0x3u));
-    out[2 * i + 1] = (uint8_t)(((w << 4) & 0x80u) | (be << 2) | (w & 0x3u));
-  }
+  for (uint64_t i = 0; i < npairs; ++i) unpack_e5m2(in[i], out + 2 * i, out + 2 * i + 1);
 }
 
 }  // extern "C"

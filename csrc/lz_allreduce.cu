@@ -15,6 +15,8 @@
 // equal to a sequential fp32 reference. Ring and RHD round to the storage
 // dtype after every hop (as NCCL does); NVLS accumulates in fp32 inside the
 // switch in a hardware-defined order.
+#include <stdlib.h>
+
 #include "lz_common.cuh"
 #include "lz_internal.h"
 
@@ -276,14 +278,21 @@ __device__ __forceinline__ void nvls_body(const LzDevComm& c, const ArParams& P)
     Range rg = slice_piece(nv, W, me, G, b);
     const uint4* src = reinterpret_cast<const uint4*>(c.heap_mc + in_off) + rg.begin;
     uint4* dst = reinterpret_cast<uint4*>(c.heap_mc + out_off) + rg.begin;
-    const size_t stride = (size_t)blockDim.x * kUnroll;
+    // P.c: loads in flight per thread (1..8); P.d bit 0: bf16 accumulation in the switch
+    const int U = P.c >= 1 && P.c <= 8 ? (int)P.c : kUnroll;
+    const bool noacc = (DT == LZ_BF16) && (P.d & 1);
+    const size_t stride = (size_t)blockDim.x * U;
     size_t i = threadIdx.x;
-    for (; i + (kUnroll - 1) * blockDim.x < rg.len; i += stride) {
-      uint4 v[kUnroll];
+    for (; i + (U - 1) * blockDim.x < rg.len; i += stride) {
+      uint4 v[8];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) v[u] = multimem_ld_reduce_v4<DT>(src + i + u * blockDim.x);
+      for (int u = 0; u < 8; ++u)
+        if (u < U)
+          v[u] = noacc ? multimem_ld_reduce_bf16_noacc(src + i + u * blockDim.x)
+                       : multimem_ld_reduce_v4<DT>(src + i + u * blockDim.x);
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) multimem_st_v4(dst + i + u * blockDim.x, v[u]);
+      for (int u = 0; u < 8; ++u)
+        if (u < U) multimem_st_v4(dst + i + u * blockDim.x, v[u]);
     }
     for (; i < rg.len; i += blockDim.x) multimem_st_v4(dst + i, multimem_ld_reduce_v4<DT>(src + i));
   }
@@ -677,10 +686,15 @@ static int plan_allreduce(const LzComm* c, const void* in, void* out, size_t cou
   }
   if (algo != LZ_ALGO_ONESHOT && algo != LZ_ALGO_NVLS_ONESHOT && (size_t)W > nv)
     algo = LZ_ALGO_ONESHOT;  // tiny vector: less than one 16-byte unit per rank
+  // Explicit grids may exceed one CTA per SM, up to what stays co-resident.
+  const int gmax = nblocks > 0 ? (c->sm_count * (2048 / nthreads) < LZ_MAX_BLOCKS
+                                      ? c->sm_count * (2048 / nthreads)
+                                      : LZ_MAX_BLOCKS)
+                               : smax;
   auto grid = [&](size_t units_per_block) {
     int G = nblocks > 0 ? nblocks
                         : clamp_int((long long)((nv / W + units_per_block - 1) / units_per_block), 1, smax);
-    return clamp_int(G, 1, smax);
+    return clamp_int(G, 1, gmax);
   };
   switch (algo) {
     case LZ_ALGO_ONESHOT:
@@ -750,6 +764,12 @@ static int plan_allreduce(const LzComm* c, const void* in, void* out, size_t cou
         copy_out = 1;
       }
       P.kind = K_NVLS;
+      {
+        const char* u = getenv("LZ_NVLS_UNROLL");
+        const char* a = getenv("LZ_NVLS_BF16_ACC");
+        P.p.c = u ? (size_t)atoi(u) : (size_t)kUnroll;
+        P.p.d = (a && atoi(a) == 0) ? 1 : 0;
+      }
       P.G = grid((size_t)nthreads * kUnroll);
       P.p.a = in_off;
       P.p.b = out_off;

@@ -170,6 +170,10 @@ int grid_for(uint64_t ntg, int nblocks) {
       return FN<DT_F32>(__VA_ARGS__);               \
     case DT_U8:                                     \
       return FN<DT_U8>(__VA_ARGS__);                \
+    case DT_E4M3P:                                  \
+      return FN<DT_E4M3P>(__VA_ARGS__);             \
+    case DT_E5M2P:                                  \
+      return FN<DT_E5M2P>(__VA_ARGS__);             \
     default:                                        \
       lz_set_error("codec: unsupported dtype %d", dt); \
       return LZE_ARG;                               \

@@ -124,6 +124,33 @@ struct Split16<DT_U8> {
   }
 };
 
+template <int DT>
+struct SplitPair16 {  // 16 fp8 pairs (32 bytes) <-> 16 container elements
+  static constexpr int IN_VECS = 2, RAW_BYTES = 16;
+  LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t* raw) {
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(v);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint16_t u = DT == DT_E4M3P ? pack_e4m3(b[2 * k], b[2 * k + 1]) : pack_e5m2(b[2 * k], b[2 * k + 1]);
+      sym[k] = sym_bf16(u);
+      raw[k] = raw_bf16(u);
+    }
+  }
+  LZ_DEV static void merge(const uint8_t* sym, const uint8_t* raw, uint4* v) {
+    uint8_t* b = reinterpret_cast<uint8_t*>(v);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint16_t u = merge_bf16(sym[k], raw[k]);
+      if (DT == DT_E4M3P) unpack_e4m3(u, &b[2 * k], &b[2 * k + 1]);
+      else unpack_e5m2(u, &b[2 * k], &b[2 * k + 1]);
+    }
+  }
+};
+template <>
+struct Split16<DT_E4M3P> : SplitPair16<DT_E4M3P> {};
+template <>
+struct Split16<DT_E5M2P> : SplitPair16<DT_E5M2P> {};
+
 // Scalar split/merge of element i (tails).
 template <int DT>
 LZ_DEV void split1(const char* in, uint32_t i, uint8_t* sym, uint8_t* raw) {
@@ -142,6 +169,12 @@ LZ_DEV void split1(const char* in, uint32_t i, uint8_t* sym, uint8_t* raw) {
     raw[0] = (uint8_t)r;
     raw[1] = (uint8_t)(r >> 8);
     raw[2] = (uint8_t)(r >> 16);
+  } else if (DT == DT_E4M3P || DT == DT_E5M2P) {
+    const uint8_t a = reinterpret_cast<const uint8_t*>(in)[2 * i];
+    const uint8_t b = reinterpret_cast<const uint8_t*>(in)[2 * i + 1];
+    const uint16_t u = DT == DT_E4M3P ? pack_e4m3(a, b) : pack_e5m2(a, b);
+    *sym = sym_bf16(u);
+    raw[0] = raw_bf16(u);
   } else {
     *sym = reinterpret_cast<const uint8_t*>(in)[i];
   }
@@ -156,6 +189,11 @@ LZ_DEV void merge1(char* out, uint32_t i, uint8_t sym, const uint8_t* raw) {
   } else if (DT == DT_F32) {
     uint32_t r = raw[0] | ((uint32_t)raw[1] << 8) | ((uint32_t)raw[2] << 16);
     reinterpret_cast<uint32_t*>(out)[i] = merge_f32(sym, r);
+  } else if (DT == DT_E4M3P || DT == DT_E5M2P) {
+    uint8_t* o = reinterpret_cast<uint8_t*>(out);
+    const uint16_t u = merge_bf16(sym, raw[0]);
+    if (DT == DT_E4M3P) unpack_e4m3(u, &o[2 * i], &o[2 * i + 1]);
+    else unpack_e5m2(u, &o[2 * i], &o[2 * i + 1]);
   } else {
     reinterpret_cast<uint8_t*>(out)[i] = sym;
   }

@@ -58,8 +58,12 @@ constexpr uint16_t VERSION = 1;
 constexpr uint8_t MODE_RAW = 0;
 constexpr uint8_t MODE_ANS = 1;
 
-// dtype codes (same values as LzDtype)
-constexpr int DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2, DT_U8 = 3;
+// dtype codes (same values as LzDtype). The two fp8 "pair" types treat two
+// consecutive fp8 bytes as one 16-bit element: the pair is packed into a
+// container whose bits 14..7 carry exponent bits of both values (symbol) and
+// whose other 8 bits (raw) carry signs and mantissas, so fp8 data needs one
+// rANS symbol per two values.
+constexpr int DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2, DT_U8 = 3, DT_E4M3P = 4, DT_E5M2P = 5;
 
 struct TgHeader {
   uint32_t magic;
@@ -93,6 +97,7 @@ LZC_HD uint32_t pad16(uint32_t x) { return (x + 15u) & ~15u; }
 LZC_HD uint64_t pad16_64(uint64_t x) { return (x + 15u) & ~uint64_t(15); }
 
 LZC_HD int elem_bytes(int dt) { return dt == DT_F32 ? 4 : (dt == DT_U8 ? 1 : 2); }
+LZC_HD bool valid_dtype(int dt) { return dt >= DT_F32 && dt <= DT_E5M2P; }
 LZC_HD int raw_bytes_per_elem(int dt) { return dt == DT_F32 ? 3 : (dt == DT_U8 ? 0 : 1); }
 
 // Worst-case record size of a TG of n elements (RAW symbol section).
@@ -125,6 +130,33 @@ LZC_HD uint8_t sym_f32(uint32_t u) { return (uint8_t)((u >> 23) & 0xFF); }
 LZC_HD uint32_t raw_f32(uint32_t u) { return (u & 0x7FFFFFu) | ((u >> 31) << 23); }
 LZC_HD uint32_t merge_f32(uint8_t s, uint32_t r) {
   return ((r >> 23) << 31) | ((uint32_t)s << 23) | (r & 0x7FFFFFu);
+}
+
+// --- fp8 pair containers ------------------------------------------------------
+// e4m3 (layout of the reference packer, back_up/fp8_e4m3fn_pack_benchmark.cu:21-31):
+//   [15]=a.sign [14:11]=a.exp [10:7]=b.exp [6:4]=a.mant [3]=b.sign [2:0]=b.mant
+LZC_HD uint16_t pack_e4m3(uint8_t a, uint8_t b) {
+  return (uint16_t)(((a & 0x80u) << 8) | ((a & 0x78u) << 8) | ((b & 0x78u) << 4) |
+                    ((a & 0x07u) << 4) | ((b & 0x80u) >> 4) | (b & 0x07u));
+}
+LZC_HD void unpack_e4m3(uint16_t w, uint8_t* a, uint8_t* b) {
+  *a = (uint8_t)(((w >> 8) & 0x80u) | ((w >> 8) & 0x78u) | ((w >> 4) & 0x07u));
+  *b = (uint8_t)(((w << 4) & 0x80u) | ((w >> 4) & 0x78u) | (w & 0x07u));
+}
+// e5m2: 5+5 exponent bits do not fit one byte; bits 14..7 carry the high four
+// exponent bits of each value, the low exponent bits move to the raw byte:
+//   [15]=a.sign [14:11]=a.e[4:1] [10:7]=b.e[4:1] [6]=a.e[0] [5:4]=a.mant
+//   [3]=b.sign [2]=b.e[0] [1:0]=b.mant
+LZC_HD uint16_t pack_e5m2(uint8_t a, uint8_t b) {
+  const uint32_t ae = (a >> 2) & 0x1Fu, be = (b >> 2) & 0x1Fu;
+  return (uint16_t)(((a & 0x80u) << 8) | ((ae >> 1) << 11) | ((be >> 1) << 7) | ((ae & 1u) << 6) |
+                    ((a & 0x3u) << 4) | ((b & 0x80u) >> 4) | ((be & 1u) << 2) | (b & 0x3u));
+}
+LZC_HD void unpack_e5m2(uint16_t w, uint8_t* a, uint8_t* b) {
+  const uint32_t ae = (((w >> 11) & 0xFu) << 1) | ((w >> 6) & 1u);
+  const uint32_t be = (((w >> 7) & 0xFu) << 1) | ((w >> 2) & 1u);
+  *a = (uint8_t)(((w >> 8) & 0x80u) | (ae << 2) | ((w >> 4) & 0x3u));
+  *b = (uint8_t)(((w << 4) & 0x80u) | (be << 2) | (w & 0x3u));
 }
 
 // --- frequency normalisation (must be identical on CPU and GPU) -------------

@@ -119,6 +119,17 @@ LZ_DEV uint4 multimem_ld_reduce_v4<LZ_F32>(const void* mc) {
   return v;
 }
 
+// bf16 reduction accumulated in bf16 by the switch (no .acc::f32): lower
+// precision, offered only as an explicit option.
+LZ_DEV uint4 multimem_ld_reduce_bf16_noacc(const void* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+
 LZ_DEV void multimem_st_v4(void* mc, uint4 v) {
   asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(mc),
                "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)

@@ -58,14 +58,26 @@ union WxSmem {
   DecSmem dec;
 };
 
-LZ_DEV int es_of(int dt) { return dt == LZ_F32 ? 4 : (dt == LZ_U8 ? 1 : 2); }
+LZ_DEV int es_of(int dt) { return dt == LZ_F32 ? 4 : (dt == LZ_U8 ? 1 : 2); }  // pairs: 2
 
 // Byte copy of `bytes` from src to dst (16-B aligned both); the tail < 16 B is
 // assembled in a register and stored as one vector (dst capacity allows it).
 template <bool kMc>
 LZ_DEV void push_bytes(char* dst, const char* src, uint32_t bytes) {
   const uint32_t full = bytes & ~15u;
-  for (uint32_t o = threadIdx.x * 16; o < full; o += blockDim.x * 16) {
+  constexpr int U = 8;  // loads in flight per thread
+  uint32_t o = threadIdx.x * 16;
+  for (; o + (U - 1) * blockDim.x * 16 < full; o += U * blockDim.x * 16) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) v[u] = ld_cg_v4(src + o + u * blockDim.x * 16);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (kMc) multimem_st_v4(dst + o + u * blockDim.x * 16, v[u]);
+      else st_v4(dst + o + u * blockDim.x * 16, v[u]);
+    }
+  }
+  for (; o < full; o += blockDim.x * 16) {
     const uint4 v = ld_cg_v4(src + o);
     if (kMc) multimem_st_v4(dst + o, v);
     else st_v4(dst + o, v);
@@ -92,6 +104,10 @@ LZ_DEV uint32_t encode_dispatch(int dt, const char* in, uint32_t n, char* dst, E
       return encode_any<DT_F16>(in, n, dst, sm);
     case LZ_BF16:
       return encode_any<DT_BF16>(in, n, dst, sm);
+    case DT_E4M3P:
+      return encode_any<DT_E4M3P>(in, n, dst, sm);
+    case DT_E5M2P:
+      return encode_any<DT_E5M2P>(in, n, dst, sm);
     default:
       return encode_any<DT_U8>(in, n, dst, sm);
   }
@@ -105,6 +121,10 @@ LZ_DEV bool decode_dispatch(int dt, const char* rec, uint32_t cap, uint32_t n, c
       return decode_tg<DT_F16>(rec, cap, n, out, sm);
     case LZ_BF16:
       return decode_tg<DT_BF16>(rec, cap, n, out, sm);
+    case DT_E4M3P:
+      return decode_tg<DT_E4M3P>(rec, cap, n, out, sm);
+    case DT_E5M2P:
+      return decode_tg<DT_E5M2P>(rec, cap, n, out, sm);
     default:
       return decode_tg<DT_U8>(rec, cap, n, out, sm);
   }
@@ -201,8 +221,15 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
       } else {
         const uint32_t bytes = d.n * (uint32_t)es_of(d.dtype);
         const uint32_t full = bytes & ~15u;
-        for (uint32_t o = threadIdx.x * 16; o < full; o += blockDim.x * 16)
-          st_v4(d.ptr + o, ld_cg_v4(slot + o));
+        uint32_t o = threadIdx.x * 16;
+        for (; o + 3 * blockDim.x * 16 < full; o += 4 * blockDim.x * 16) {
+          uint4 v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) v[u] = ld_cg_v4(slot + o + u * blockDim.x * 16);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) st_v4(d.ptr + o + u * blockDim.x * 16, v[u]);
+        }
+        for (; o < full; o += blockDim.x * 16) st_v4(d.ptr + o, ld_cg_v4(slot + o));
         if (threadIdx.x < bytes - full) d.ptr[full + threadIdx.x] = (char)ld_cg_u8(slot + full + threadIdx.x);
       }
       __syncthreads();
@@ -249,7 +276,8 @@ extern "C" int lz_weight_transfer(LzComm* c, int role, int src, unsigned int rec
   p.src = src;
   p.recv_mask = recv_mask;
   const bool all = broadcast_all && recv_mask == (((1u << W) - 1u) & ~(1u << src));
-  p.use_mc = (all && c->dev.heap_mc) ? 1 : 0;
+  // one receiver: direct peer stores beat a multicast write that also lands locally
+  p.use_mc = (all && W > 2 && c->dev.heap_mc) ? 1 : 0;
   p.kslots = kslots;
   p.cap = tg_capacity(LZ_F32);
   p.slots_off = c->stage_off;

@@ -78,6 +78,17 @@ def _as_bytes_view(t: torch.Tensor) -> torch.Tensor:
     return t
 
 
+DT_E4M3P, DT_E5M2P = 4, 5
+FP8_PAIRS = True  # code fp8 data as packed pairs (one rANS symbol per two values)
+
+
+def plan(t_dtype: torch.dtype, numel: int):
+    """(codec dtype code, codec element count) for a tensor of `numel` values."""
+    if t_dtype in _fp8_types() and FP8_PAIRS and numel % 2 == 0:
+        return (DT_E4M3P if t_dtype == torch.float8_e4m3fn else DT_E5M2P), numel // 2
+    return codec_dtype(t_dtype), numel
+
+
 def tg_capacity(dtype: torch.dtype) -> int:
     return int(_native.cpu().lzc_tg_capacity(TG_ELEMS, codec_dtype(dtype)))
 
@@ -89,10 +100,10 @@ def max_encoded_bytes(n: int, dtype: torch.dtype) -> int:
 # ----------------------------------------------------------------------------- CPU oracle
 def encode_cpu(t: torch.Tensor) -> torch.Tensor:
     """Compact LZC1 stream of a contiguous CPU tensor (uint8 tensor)."""
-    t = _as_bytes_view(t.detach().contiguous().cpu())
-    n = t.numel()
-    dt = codec_dtype(t.dtype)
-    cap = max_encoded_bytes(n, t.dtype)
+    t = t.detach().contiguous().cpu()
+    dt, n = plan(t.dtype, t.numel())
+    t = _as_bytes_view(t)
+    cap = int(_native.cpu().lzc_max_stream_bytes(n, dt))
     out = torch.empty(cap, dtype=torch.uint8)
     rc = _native.cpu().lzc_encode(t.data_ptr(), n, dt, out.data_ptr(), cap)
     if rc < 0:
@@ -102,10 +113,10 @@ def encode_cpu(t: torch.Tensor) -> torch.Tensor:
 
 def decode_cpu(blob: torch.Tensor, n: int, dtype: torch.dtype) -> torch.Tensor:
     blob = blob.contiguous().cpu()
-    dt = codec_dtype(dtype)
+    dt, ne = plan(dtype, n)
     store = torch.uint8 if dtype in _fp8_types() else dtype
     out = torch.empty(n, dtype=store)
-    rc = _native.cpu().lzc_decode(blob.data_ptr(), blob.numel(), out.data_ptr(), n, dt)
+    rc = _native.cpu().lzc_decode(blob.data_ptr(), blob.numel(), out.data_ptr(), ne, dt)
     if rc != 0:
         raise CodecError(f"corrupt LZC1 stream (code {rc})")
     return out.view(dtype) if store != dtype else out
@@ -156,8 +167,9 @@ def encode(t: torch.Tensor, nblocks: int = 0, stream=None, return_size: bool = T
     if not t.is_cuda:
         return encode_cpu(t)
     L = _native.cuda()
-    t = _as_bytes_view(t.contiguous())
-    n, dt = t.numel(), codec_dtype(t.dtype)
+    t = t.contiguous()
+    dt, n = plan(t.dtype, t.numel())
+    t = _as_bytes_view(t)
     cap = L.lz_codec_max_bytes(n, dt)
     scratch = torch.empty(L.lz_codec_scratch_bytes(n, dt), dtype=torch.uint8, device=t.device)
     out = torch.empty(cap, dtype=torch.uint8, device=t.device)
@@ -183,7 +195,8 @@ def decode(blob: torch.Tensor, like: torch.Tensor | None = None, n: int | None =
     if out is None:
         out = torch.empty(n, dtype=store, device=blob.device)
     status = torch.zeros(1, dtype=torch.int32, device=blob.device)
-    _native.check(L.lz_codec_decode(blob.data_ptr(), blob.numel(), out.data_ptr(), n, codec_dtype(dtype),
+    dtc, ne = plan(dtype, n)
+    _native.check(L.lz_codec_decode(blob.data_ptr(), blob.numel(), out.data_ptr(), ne, dtc,
                                     status.data_ptr(), nblocks, _stream_ptr(stream)), "lz_codec_decode")
     if check:
         st = int(status.item())

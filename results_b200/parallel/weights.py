@@ -31,7 +31,7 @@ import torch
 import torch.distributed as dist
 
 from .. import _native, _native_sigs
-from ..utils.dtypes import lz_dtype
+from ..ops import codec
 
 _native_sigs.add_cuda({
     "lz_wx_slot_capacity": (C.c_size_t,),
@@ -56,14 +56,14 @@ def build_descriptors(tensors, encode, device) -> tuple[torch.Tensor, int]:
     for t, enc in zip(tensors, encode):
         if not t.is_contiguous():
             raise ValueError("weight transfer needs contiguous tensors")
-        numel = t.numel()
-        if numel == 0:
+        if t.numel() == 0:
             continue
-        es = t.element_size()
         base = t.data_ptr()
         if base % 16:
             raise ValueError("weight transfer needs 16-byte aligned tensors")
-        dt = lz_dtype(t.dtype) if t.dtype in (torch.float32, torch.float16, torch.bfloat16) else 3
+        # fp8 tensors of even length travel as packed pairs (fused pack/unpack)
+        dt, numel = codec.plan(t.dtype, t.numel())
+        es = 4 if dt == 0 else (1 if dt == 3 else 2)
         ntg = (numel + TG - 1) // TG
         idx = torch.arange(ntg, dtype=torch.int64)
         rows_ptr.append(base + idx * (TG * es))
