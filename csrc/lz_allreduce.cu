@@ -1001,3 +1001,26 @@ extern "C" int lz_emu_allreduce(LzEmu* e, const void* const* ins, void* const* o
   LZ_CUDA_TRY(cudaStreamSynchronize(s));  // hp lives on this stack frame
   return LZE_OK;
 }
+
+// ----------------------------------------------------------------------------
+// Test hook: one block waits on a local flag word that nothing sets, with the
+// communicator's bounded wait. The kernel must give up after timeout_ns and
+// report LZ_ERR_TIMEOUT through the host-mapped status word; the context
+// stays usable. No other rank is involved.
+// ----------------------------------------------------------------------------
+namespace {
+__global__ void wait_never_set_kernel(LzDevComm c, unsigned long long* flag) {
+  if (threadIdx.x == 0) lz_wait_ge(c, flag, 1ull, 9, c.rank);
+}
+}  // namespace
+
+extern "C" int lz_test_wait_timeout(LzComm* c, double timeout_s, cudaStream_t s) {
+  LzDevComm d = c->dev;
+  d.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  // a flag word in the reserved part of this rank's flag area, zeroed here
+  unsigned long long* flag = reinterpret_cast<unsigned long long*>(c->dev.heap[c->dev.rank] + (512u << 10));
+  LZ_CUDA_TRY(cudaMemsetAsync(flag, 0, 8, s));
+  wait_never_set_kernel<<<1, 32, 0, s>>>(d, flag);
+  LZ_CUDA_TRY(cudaGetLastError());
+  return LZE_OK;
+}

@@ -21,6 +21,8 @@ _CUDA = {
     "lz_emu_allreduce": (c_int, c_ptr, P(c_ptr), P(c_ptr), c_size, c_int, c_int, c_int, c_int, c_ptr),
 }
 
+_CUDA["lz_test_wait_timeout"] = (c_int, c_ptr, c_dbl, c_ptr)
+
 _CPU = {}
 
 

@@ -213,6 +213,28 @@ class Communicator:
                 f"rank {self.rank}: device wait failed (code {code}) in phase {phase} "
                 f"waiting for rank {peer} (block {block}); communicator must be recreated")
 
+    def test_wait_timeout(self, timeout_s: float = 0.2) -> None:
+        """Launch a kernel whose bounded wait must expire (failure-path test hook)."""
+        s = torch.cuda.current_stream(self.device)
+        _native.check(self._lib.lz_test_wait_timeout(self._comm, C.c_double(timeout_s), s.cuda_stream),
+                      "test wait")
+
+    def clear_status(self) -> None:
+        self._lib.lz_comm_clear_status(self._comm)
+
+    def attach_heartbeat(self, period_s: float = 0.2):
+        """Start publishing liveness in the store; `guard()` then checks peers."""
+        from ..utils.health import Heartbeat
+
+        self._hb = Heartbeat(self.rank, self.world, period_s=period_s)
+        return self._hb
+
+    def guard(self, max_age_s: float = 2.0) -> None:
+        """Raise PeerLost before launching if a peer left or stopped heart-beating."""
+        hb = getattr(self, "_hb", None)
+        if hb is not None:
+            hb.check(max_age_s)
+
     def epoch(self) -> int:
         v = C.c_uint64()
         s = torch.cuda.current_stream(self.device)
@@ -220,6 +242,25 @@ class Communicator:
         return v.value
 
     # ------------------------------------------------------------ teardown
+    def abandon(self) -> None:
+        """Local, non-collective teardown for failure paths (no peer barrier).
+
+        Only call when none of this rank's kernels are in flight. Peers keep
+        their own imports of this rank's memory alive until they tear down.
+        """
+        if self._closed:
+            return
+        self._closed = True
+        try:
+            torch.cuda.synchronize(self.device)
+        except Exception:
+            pass
+        hb = getattr(self, "_hb", None)
+        if hb is not None:
+            hb.stop()
+        self._lib.lz_comm_destroy(self._comm)
+        self._lib.lz_heap_destroy(self._heap)
+
     def close(self) -> None:
         """Collective teardown: barrier, then unmap peers and unbind multicast."""
         if self._closed:

@@ -1,0 +1,59 @@
+"""Host-side tools: log parsers, launcher command, SVG plots, CSV schemas, config."""
+import csv
+import os
+
+from results_b200.utils import csvfmt, logparse, plots
+
+
+def test_logparse_reference_and_own_lines():
+    lines = [
+        "[E] DietGPUCompressorBackend: Compressed 1048576 bytes to 700000 bytes, ratio 0.6676 weight=q_proj",
+        "[E] DietGPUCompressorBackend: Compressed 1048576 bytes to 702000 bytes, ratio 0.6695 weight=q_proj",
+        logparse.log_line("mlp.down_proj.weight", 2000, 1350),
+        "unrelated line",
+    ]
+    s = logparse.by_size(lines)
+    assert abs(s[1048576] - (700000 + 702000) / 2 / 1048576) < 1e-9
+    w = logparse.by_weight(lines)
+    assert "q_proj" in w and "mlp.down_proj.weight" in w
+
+
+def test_launch_command():
+    from results_b200.launch import build_command
+
+    cmd = build_command("local", 8, ["bench.py", "--gpus", "8"], master_port=29555)
+    assert "--nproc-per-node=8" in cmd and "--master-addr=127.0.0.1" in cmd and cmd[:2] == ["timeout", "-k"]
+    cmd2 = build_command("node", 8, ["x.py"], nnodes=2, node_rank=1, master_addr="10.0.0.2", master_port=1)
+    assert "--nnodes=2" in cmd2 and "--node-rank=1" in cmd2
+
+
+def test_schema_a_csv_and_chart(tmp_path):
+    rows = []
+    for v, base in (("P2P", 1.0), ("NVLS", 1.2)):
+        for s in (1 << 20, 1 << 24, 1 << 30):
+            for m in ("wall_ms", "cuda_ms"):
+                rows.append({"metric": m, "size_label": csvfmt.size_label(s), "size_bytes": s, "world_size": 8,
+                             "variant": v, "nccl_ms": 1.0, "variant_ms": base, "variant_vs_nccl_pct": 100,
+                             "nccl_algbw_GBps": 1, "variant_algbw_GBps": s / base / 1e6,
+                             "nccl_busbw_GBps": 1, "variant_busbw_GBps": s / base / 1e6 * 1.75, "comp_ratio": ""})
+    p = str(tmp_path / "a.csv")
+    csvfmt.write_rows(p, csvfmt.SCHEMA_A, rows, blocks=[[r for r in rows if r["metric"] == "wall_ms"],
+                                                       [r for r in rows if r["metric"] == "cuda_ms"]])
+    with open(p) as f:
+        assert f.readline().strip().split(",") == csvfmt.SCHEMA_A
+    svg = plots.sweep_chart(p, str(tmp_path / "a.svg"))
+    assert open(svg).read().startswith("<svg")
+
+
+def test_config_env(monkeypatch):
+    from results_b200.config import Config
+
+    monkeypatch.setenv("LZ_TIMEOUT_S", "3.5")
+    monkeypatch.setenv("RING_NUM_CHANNELS", "2")
+    monkeypatch.setenv("HD_MAX_MB", "64")
+    c = Config.from_env()
+    assert c.timeout_s == 3.5 and c.ring_channels == 2 and c.hd_max_bytes == 64 << 20
+
+
+def test_size_labels():
+    assert csvfmt.size_label(1 << 30) == "1 GB" and csvfmt.size_label(1024) == "1 KB"
