@@ -669,7 +669,20 @@ static int plan_allreduce(const LzComm* c, const void* in, void* out, size_t cou
   const size_t es = (DT == LZ_F32) ? 4 : 2;
   const size_t bytes = count * es;
   const size_t nv = bytes / 16;
-  if (nthreads <= 0) nthreads = 512;
+  // Launch shape measured on 8xB200 (1 GiB: NVLS 256 threads x 4 loads in
+  // flight = 809 GB/s busbw; 64 MB: 512 threads x 8 in flight): used when the
+  // caller does not force one (nthreads <= 0).
+  const bool auto_shape = nthreads <= 0;
+  int nvls_unroll = 8;
+  if (auto_shape) {
+    nthreads = 512;
+    if (algo == LZ_ALGO_NVLS && bytes >= (128u << 20)) {
+      nthreads = 256;
+      nvls_unroll = 4;
+    }
+  } else {
+    nvls_unroll = kUnroll;
+  }
   nthreads = clamp_int(nthreads, 32, 512) / 32 * 32;
   const int smax = c->sm_count < LZ_MAX_BLOCKS ? c->sm_count : LZ_MAX_BLOCKS;
   ArPlan P;
@@ -767,7 +780,7 @@ static int plan_allreduce(const LzComm* c, const void* in, void* out, size_t cou
       {
         const char* u = getenv("LZ_NVLS_UNROLL");
         const char* a = getenv("LZ_NVLS_BF16_ACC");
-        P.p.c = u ? (size_t)atoi(u) : (size_t)kUnroll;
+        P.p.c = u ? (size_t)atoi(u) : (size_t)nvls_unroll;
         P.p.d = (a && atoi(a) == 0) ? 1 : 0;
       }
       P.G = grid((size_t)nthreads * kUnroll);

@@ -319,6 +319,13 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
   __syncthreads();
   // 1. split + histogram (+ raw plane straight to the destination)
   const uint32_t units = n / 16;
+  // software-pipelined: the vectors of the next unit are loaded before the
+  // current one is split and counted
+  uint4 nxt[S::IN_VECS];
+  if (tid < units) {
+#pragma unroll
+    for (int q = 0; q < S::IN_VECS; ++q) nxt[q] = ld_cg_v4(in + (size_t)tid * 16 * ES + 16 * q);
+  }
   for (uint32_t u0 = 0; u0 < units; u0 += blockDim.x) {  // block-uniform trip count
     const uint32_t u = u0 + tid;
     const bool act = u < units;
@@ -326,7 +333,12 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
     if (act) {
       uint4 v[S::IN_VECS];
 #pragma unroll
-      for (int q = 0; q < S::IN_VECS; ++q) v[q] = ld_cg_v4(in + (size_t)u * 16 * ES + 16 * q);
+      for (int q = 0; q < S::IN_VECS; ++q) v[q] = nxt[q];
+      const uint32_t un = u + blockDim.x;
+      if (un < units) {
+#pragma unroll
+        for (int q = 0; q < S::IN_VECS; ++q) nxt[q] = ld_cg_v4(in + (size_t)un * 16 * ES + 16 * q);
+      }
       uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 1];
       S::split(v, sy, rw);
       *reinterpret_cast<uint4*>(&sm.syms[u * 16]) = *reinterpret_cast<const uint4*>(sy);
@@ -495,8 +507,18 @@ LZ_DEV bool decode_tg_syms(const char* __restrict__ src, uint32_t cap, uint32_t 
     const uint32_t nnz = sm.h.nnz, nsub = sm.h.nsub;
     // stage the whole ANS section (<= pad16(n) bytes) so every word fetch of
     // the rANS loop is a shared-memory load, off the global-latency path
-    for (uint32_t o = tid * 16; o < sm.h.sym_bytes; o += blockDim.x * 16)
-      *reinterpret_cast<uint4*>(&sm.sec[o]) = ld_cg_v4(symsec + o);
+    {
+      const uint32_t sb = sm.h.sym_bytes, step = blockDim.x * 16;
+      uint32_t o = tid * 16;
+      for (; o + 3 * step < sb; o += 4 * step) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = ld_cg_v4(symsec + o + u * step);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(&sm.sec[o + u * step]) = v[u];
+      }
+      for (; o < sb; o += step) *reinterpret_cast<uint4*>(&sm.sec[o]) = ld_cg_v4(symsec + o);
+    }
     __syncthreads();
     symsec = reinterpret_cast<const char*>(sm.sec);
     // decode table: slot -> entry, by binary search over the cumulative table

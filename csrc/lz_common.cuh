@@ -49,39 +49,20 @@ LZ_DEV void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 LZ_DEV void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
 // 16-byte global loads/stores. `cg` bypasses L1 for data another GPU wrote.
-LZ_DEV uint4 ld_cg_v4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-LZ_DEV uint4 ld_nc_v4(const void* p) {  // read-only for the kernel's lifetime
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
+// These are compiler intrinsics, not volatile asm, so loads of later loop
+// iterations can be scheduled early; ordering against flag waits is kept
+// because those are volatile asm with memory clobbers.
+LZ_DEV uint4 ld_cg_v4(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+LZ_DEV uint4 ld_nc_v4(const void* p) {  // read-only for the kernel's lifetime, streamed
+  return __ldcs(reinterpret_cast<const uint4*>(p));
 }
 LZ_DEV uint8_t ld_cg_u8(const void* p) {
-  unsigned short v;
-  asm volatile("ld.global.cg.u8 %0, [%1];" : "=h"(v) : "l"(p));
-  return (uint8_t)v;
+  return (uint8_t)__ldcg(reinterpret_cast<const unsigned char*>(p));
 }
-LZ_DEV uint32_t ld_cg_u32(const void* p) {
-  uint32_t v;
-  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
-LZ_DEV void st_v4(void* p, uint4 v) {
-  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
-               "r"(v.z), "r"(v.w)
-               : "memory");
-}
+LZ_DEV uint32_t ld_cg_u32(const void* p) { return __ldcg(reinterpret_cast<const unsigned int*>(p)); }
+LZ_DEV void st_v4(void* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
 LZ_DEV void st_cs_v4(void* p, uint4 v) {  // streaming store (evict-first)
-  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
-               "r"(v.z), "r"(v.w)
-               : "memory");
+  __stcs(reinterpret_cast<uint4*>(p), v);
 }
 
 // ----------------------------------------------------------------------------

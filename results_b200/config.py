@@ -52,7 +52,7 @@ class Config:
     # device waits
     timeout_s: float = 10.0
     # launch shape
-    nthreads: int = 512
+    nthreads: int = 0                 # 0: per-algorithm launch shape measured on B200
     sm_budget: int = 0                # 0: all SMs; otherwise the grid is capped to this
     # algorithm selection (bytes); measured on 8xB200, see results_b200/parallel/tuning.py
     algo: str = "auto"

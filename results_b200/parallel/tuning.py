@@ -11,10 +11,18 @@ from __future__ import annotations
 KiB = 1 << 10
 MiB = 1 << 20
 
-# world -> list of (max_bytes, algo_with_multicast, algo_without_multicast)
+# world -> list of (max_bytes, algo_with_multicast, algo_without_multicast).
+# 2 GPUs (sweep of 2xB200, bf16): one-shot wins up to 8 MB, two-shot above
+# (NVLS moves (1 + 1/N) S per GPU but is slower than two-shot's S at N = 2).
+# 8 GPUs: NVLS wins from 64 MB (621 vs 517 two-shot, NCCL 421) to 1 GB
+# (809 vs 646, NCCL 725).
 TABLE = {
+    2: [
+        (8 * MiB, "oneshot", "oneshot"),
+        (1 << 62, "twoshot", "twoshot"),
+    ],
     "default": [
-        (256 * KiB, "oneshot", "oneshot"),
+        (4 * MiB, "oneshot", "oneshot"),
         (1 << 62, "nvls", "twoshot"),
     ],
 }
