@@ -296,3 +296,103 @@ extern "C" int lz_weight_transfer(LzComm* c, int role, int src, unsigned int rec
   LZ_CUDA_TRY(cudaLaunchKernel(fn, dim3(G), dim3(LZC_THREADS), args, smem, s));
   return LZE_OK;
 }
+
+// ----------------------------------------------------------------------------
+// Zero-copy raw transfer into symmetric destinations. Receivers' tensors live
+// in the symmetric heap at the same offsets on every rank, so the sender
+// writes each table group straight into every receiver's tensor: one
+// multimem.st per 16 bytes through the switch when every other rank receives,
+// peer stores otherwise. No slots, credits or receiver copies; each sender
+// CTA raises one completion flag per receiver at the end, and receiver CTA b
+// waits for the flag of sender CTA b.
+// ----------------------------------------------------------------------------
+namespace {
+
+struct WxDirectDesc {
+  const char* src;  // sender: source bytes (unused on receivers)
+  uint64_t dst_off; // heap offset of the destination bytes (same on every rank)
+  uint64_t bytes;
+  uint64_t pad;
+};
+static_assert(sizeof(WxDirectDesc) == 32, "direct descriptor layout");
+
+struct WxDirectParams {
+  const WxDirectDesc* descs;
+  uint32_t ndesc;
+  int role;
+  int src;
+  uint32_t recv_mask;
+  int use_mc;
+  size_t ready_off;
+  unsigned long long seq[LZ_MAX_RANKS];
+};
+
+constexpr uint64_t kDirectChunk = 256u << 10;  // bytes per work item
+
+__global__ void __launch_bounds__(256) wx_direct_kernel(LzDevComm c, WxDirectParams p) {
+  const int W = c.world, G = gridDim.x, b = blockIdx.x;
+  if (p.role == 0) {
+    // work items: 256 KB chunks of every descriptor, dealt round-robin to CTAs
+    uint64_t item = 0;
+    for (uint32_t k = 0; k < p.ndesc; ++k) {
+      const WxDirectDesc d = p.descs[k];
+      const uint64_t nchunks = (d.bytes + kDirectChunk - 1) / kDirectChunk;
+      for (uint64_t ch = 0; ch < nchunks; ++ch, ++item) {
+        if (item % G != (uint64_t)b) continue;
+        const uint64_t off = ch * kDirectChunk;
+        const uint32_t len = (uint32_t)min(kDirectChunk, d.bytes - off);
+        if (p.use_mc) {
+          push_bytes<true>(c.heap_mc + d.dst_off + off, d.src + off, len);
+        } else {
+          for (int r = 0; r < W; ++r)
+            if ((p.recv_mask >> r) & 1u) push_bytes<false>(c.heap[r] + d.dst_off + off, d.src + off, len);
+        }
+      }
+    }
+    __syncthreads();
+    const int t = threadIdx.x;
+    if (t < W && ((p.recv_mask >> t) & 1u)) {
+      fence_sys();
+      unsigned long long* f = reinterpret_cast<unsigned long long*>(c.heap[t] + p.ready_off) +
+                              (size_t)p.src * LZ_MAX_BLOCKS + b;
+      st_release_sys(f, p.seq[t] | 1ull);
+    }
+  } else {
+    if (threadIdx.x == 0) {
+      const unsigned long long* f = reinterpret_cast<const unsigned long long*>(c.heap[c.rank] + p.ready_off) +
+                                    (size_t)p.src * LZ_MAX_BLOCKS + b;
+      lz_wait_ge(c, f, p.seq[0] | 1ull, 8, p.src);
+      fence_proxy_alias();
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int lz_weight_transfer_direct(LzComm* c, int role, int src, unsigned int recv_mask,
+                                         const void* descs, unsigned int ndesc, int nblocks,
+                                         int broadcast_all, const unsigned long long* seqs,
+                                         cudaStream_t s) {
+  const int W = c->dev.world;
+  if (W == 1 || ndesc == 0) return LZE_OK;
+  if (src < 0 || src >= W || (recv_mask >> src) & 1u || recv_mask == 0 || (recv_mask >> W) != 0u) {
+    lz_set_error("direct weight transfer: bad src %d / receiver mask 0x%x", src, recv_mask);
+    return LZE_ARG;
+  }
+  int G = nblocks > 0 ? nblocks : c->sm_count * 2;
+  if (G > LZ_MAX_BLOCKS) G = LZ_MAX_BLOCKS;
+  WxDirectParams p;
+  memset(&p, 0, sizeof(p));
+  p.descs = static_cast<const WxDirectDesc*>(descs);
+  p.ndesc = ndesc;
+  p.role = role;
+  p.src = src;
+  p.recv_mask = recv_mask;
+  const bool all = broadcast_all && recv_mask == (((1u << W) - 1u) & ~(1u << src));
+  p.use_mc = (all && W > 2 && c->dev.heap_mc) ? 1 : 0;
+  p.ready_off = all ? kReadyB : kReadyP;
+  for (int r = 0; r < LZ_MAX_RANKS; ++r) p.seq[r] = seqs[r] << 32;
+  wx_direct_kernel<<<G, 256, 0, s>>>(c->dev, p);
+  LZ_CUDA_TRY(cudaGetLastError());
+  return LZE_OK;
+}

@@ -7,6 +7,8 @@ Modes
   ours_raw     native transfer, raw bytes (NVLS multimem broadcast when every rank receives)
   ours_split   native transfer, split+rANS encoded (bit-exact), same paths
   ours_p2p     native point-to-point transfer to each receiver in turn (split+rANS)
+  ours_direct  native zero-copy raw broadcast into receivers' symmetric weight tensors
+               (one multimem.st per 16 bytes reaches every receiver's weights)
   nccl_bcast   per-tensor torch.distributed.broadcast, the reference's update path
                (back_up/update_weight_from_distributed.py:422-449)
   nccl_send    per-tensor send from rank 0 to every receiver (batched isend/irecv)
@@ -75,10 +77,14 @@ def main():
     fn = shapes.MODELS[a.model]
     specs = fn(layers=a.layers) if a.layers else fn()
     total_bytes = shapes.total_params(specs) * 2
-    comm = lz.init(config=Config(user_bytes=64 * MiB, stage_bytes=512 * MiB, timeout_s=60.0))
+    direct = "ours_direct" in a.modes
+    user = (total_bytes + 256 * MiB) if direct else 64 * MiB
+    comm = lz.init(config=Config(user_bytes=user, stage_bytes=512 * MiB, timeout_s=60.0))
     sd = shapes.make_state_dict(specs, seed=1, empty=(rank != 0))
     names = list(sd.keys())
     tensors = list(sd.values())
+    sym = [comm.empty(t.shape, t.dtype) for t in tensors] if direct else None  # collective, same offsets
+    sym_of = {id(t): d for t, d in zip(tensors, sym)} if direct else {}
     bucket = a.bucket_mb * MiB
     engines = {
         "ours_raw": weights.WeightTransfer(comm, mode="raw"),
@@ -87,6 +93,10 @@ def main():
     }
 
     def run(mode, ts):
+        if mode == "ours_direct":
+            dst = [sym_of[id(t)] for t in ts]
+            engines["ours_raw"].broadcast_direct(dst, 0, src_tensors=ts if rank == 0 else None)
+            return
         if mode in ("ours_raw", "ours_split"):
             eng = engines[mode]
             for bkt in weights.buckets(list(zip(range(len(ts)), ts)), bucket):
@@ -125,7 +135,7 @@ def main():
         if world == 1:
             break
         if rank != 0:
-            for t in tensors:
+            for t in (sym if mode == "ours_direct" else tensors):
                 t.fill_(0)
         for _ in range(a.warmup):
             run(mode, tensors)
@@ -144,7 +154,8 @@ def main():
         comm.check()
         ok = True
         if rank != 0:
-            ok = all(checksum(t) == s for t, s in zip(tensors, ref_sums))
+            got = sym if mode == "ours_direct" else tensors
+            ok = all(checksum(t) == s for t, s in zip(got, ref_sums))
         okt = torch.tensor([0 if ok else 1])
         dist.all_reduce(okt, group=ctrl)
         results[mode] = {"sec": sec, "wall_sec": wall, "bitexact": int(okt.item()) == 0,
@@ -183,11 +194,11 @@ def main():
         summary = {"model": a.model, "params": shapes.total_params(specs), "bytes": total_bytes, "world": world,
                    "multicast": comm.has_multicast, "results": results}
         if "nccl_send" in results:
-            for m in ("ours_raw", "ours_split"):
+            for m in ("ours_raw", "ours_split", "ours_direct"):
                 if m in results:
                     summary[f"speedup_{m}_vs_nccl_send"] = results["nccl_send"]["sec"] / results[m]["sec"]
         if "nccl_bcast" in results:
-            for m in ("ours_raw", "ours_split"):
+            for m in ("ours_raw", "ours_split", "ours_direct"):
                 if m in results:
                     summary[f"speedup_{m}_vs_nccl_bcast"] = results["nccl_bcast"]["sec"] / results[m]["sec"]
         print(json.dumps(summary), flush=True)

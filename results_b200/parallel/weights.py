@@ -39,6 +39,8 @@ _native_sigs.add_cuda({
     "lz_wx_stage_bytes": (C.c_size_t, C.c_int, C.c_int),
     "lz_weight_transfer": (C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_uint, C.c_void_p, C.c_uint, C.c_int,
                            C.c_int, C.c_int, C.POINTER(C.c_uint64), C.c_void_p),
+    "lz_weight_transfer_direct": (C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_uint, C.c_void_p, C.c_uint,
+                                  C.c_int, C.c_int, C.POINTER(C.c_uint64), C.c_void_p),
 })
 
 TG = 32768
@@ -157,6 +159,52 @@ class WeightTransfer:
             self.pair_seq[(src, me)] = s
             mask = 1 << me
         self._launch(1, src, mask, descs, ntg, broadcast_all, [s] * 8)
+        self._keep = descs
+
+    # ------------------------------------------------------------ zero-copy raw
+    def _direct_descs(self, dst_tensors, src_tensors):
+        comm = self.comm
+        rows = []
+        for i, d in enumerate(dst_tensors):
+            if not comm.is_symmetric(d):
+                raise ValueError("direct transfer needs destination tensors allocated with comm.empty()")
+            srcp = src_tensors[i].data_ptr() if src_tensors is not None else 0
+            if src_tensors is not None and (src_tensors[i].numel() * src_tensors[i].element_size()
+                                            != d.numel() * d.element_size()):
+                raise ValueError("source and destination sizes differ")
+            rows.append([srcp, d.data_ptr() - comm._local_base, d.numel() * d.element_size(), 0])
+        t = torch.tensor(rows, dtype=torch.int64).pin_memory()
+        return t.to(f"cuda:{comm.device}", non_blocking=True), len(rows)
+
+    def broadcast_direct(self, dst_tensors, src: int, src_tensors=None, nblocks: int = 0) -> None:
+        """Zero-copy raw broadcast into symmetric destination tensors.
+
+        Every rank passes its symmetric destination tensors (allocated with
+        ``comm.empty`` in the same order on all ranks); the sender also passes
+        ``src_tensors`` (default: its own destination tensors). One multimem
+        store per 16 bytes lands in every receiver's tensor.
+        """
+        comm = self.comm
+        if comm.world == 1:
+            if src_tensors is not None:
+                for d, s_ in zip(dst_tensors, src_tensors):
+                    d.copy_(s_)
+            return
+        me = comm.rank
+        mask = ((1 << comm.world) - 1) & ~(1 << src)
+        s = self.bcast_seq.get(src, 0) + 1
+        self.bcast_seq[src] = s
+        if me == src:
+            descs, nd = self._direct_descs(dst_tensors, src_tensors if src_tensors is not None else dst_tensors)
+            role = 0
+        else:
+            descs, nd = self._direct_descs(dst_tensors, None)
+            role = 1
+        arr = (C.c_uint64 * 8)(*([s] * 8))
+        st = torch.cuda.current_stream(comm.device)
+        rc = comm._lib.lz_weight_transfer_direct(comm.handle, role, src, mask, descs.data_ptr(), nd,
+                                                 nblocks or min(comm.sm_count * 2, 512), 1, arr, st.cuda_stream)
+        _native.check(rc, "direct weight transfer")
         self._keep = descs
 
     def broadcast(self, tensors, src: int) -> None:

@@ -47,6 +47,18 @@ def _worker(rank, world, cases, dump_dir):
         comm.check()
         ok = all(torch.equal(sd[k].view(torch.int16), ref[k].view(torch.int16)) for k in ref)
         results.append((mode, kind, frac, ok))
+    # zero-copy raw broadcast into symmetric destinations
+    comm.reset_alloc()
+    sym = [comm.empty(t.shape, t.dtype) for t in ref.values()]
+    for t in sym:
+        t.fill_(-3)
+    wt = weights.WeightTransfer(comm, mode="raw")
+    for _ in range(2):
+        wt.broadcast_direct(sym, 0, src_tensors=list(ref.values()) if rank == 0 else None, nblocks=32)
+    torch.cuda.synchronize()
+    comm.check()
+    results.append(("raw", "direct", 0.0, all(torch.equal(a.view(torch.int16), b.view(torch.int16))
+                                              for a, b in zip(sym, ref.values()))))
     # dump oracle: rank 0 dumps, the others compare what they received with it
     if rank == 0:
         weights.dump_tensors(list(ref.items()), dump_dir, 3, 0, group_name="test")
