@@ -6,6 +6,8 @@
 // reports corruption through a status word instead of trapping (the
 // reference's codec asserted on a bad header, raw/a.txt:290-320 of the
 // reference).
+#include <stdlib.h>
+
 #include <cub/block/block_scan.cuh>
 
 #include "lz_codec_dev.cuh"
@@ -20,7 +22,7 @@ template <int DT>
 __global__ void __launch_bounds__(LZC_THREADS) encode_slotted_kernel(const char* __restrict__ in,
                                                                       uint64_t n, char* slots,
                                                                       uint32_t slot_cap,
-                                                                      uint32_t* sizes) {
+                                                                      uint32_t* sizes, int stop_after) {
   extern __shared__ __align__(16) char smem_raw[];
   EncSmem& sm = *reinterpret_cast<EncSmem*>(smem_raw);
   constexpr int ES = DT == DT_F32 ? 4 : (DT == DT_U8 ? 1 : 2);
@@ -28,7 +30,7 @@ __global__ void __launch_bounds__(LZC_THREADS) encode_slotted_kernel(const char*
   for (uint64_t t = blockIdx.x; t < ntg; t += gridDim.x) {
     const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, n - t * TG_ELEMS);
     const uint32_t bytes =
-        encode_tg<DT>(in + t * (uint64_t)TG_ELEMS * ES, tn, slots + t * (uint64_t)slot_cap, sm);
+        encode_tg<DT>(in + t * (uint64_t)TG_ELEMS * ES, tn, slots + t * (uint64_t)slot_cap, sm, stop_after);
     if (threadIdx.x == 0) sizes[t] = bytes;
   }
 }
@@ -190,8 +192,9 @@ int launch_encode_slotted(const void* in, uint64_t n, void* slots, uint32_t* siz
   }
   int rc = prep_smem(encode_slotted_kernel<DT>, sizeof(EncSmem));
   if (rc) return rc;
+  static const int stop_after = getenv("LZ_CODEC_STOP_AFTER") ? atoi(getenv("LZ_CODEC_STOP_AFTER")) : 0;
   encode_slotted_kernel<DT><<<grid_for(ntg, nblocks), LZC_THREADS, sizeof(EncSmem), s>>>(
-      static_cast<const char*>(in), n, static_cast<char*>(slots), tg_capacity(DT), sizes);
+      static_cast<const char*>(in), n, static_cast<char*>(slots), tg_capacity(DT), sizes, stop_after);
   LZ_CUDA_TRY(cudaGetLastError());
   return LZE_OK;
 }

@@ -305,9 +305,11 @@ LZ_DEV void build_tables_warp0(EncSmem& sm, uint32_t n) {
 // `dst` (16-B aligned; any memory the CTA can store to: local, peer).
 // Returns the record size (uniform over the CTA).
 // ---------------------------------------------------------------------------
+// `stop_after` (profiling only): 1 = split + histogram, 2 = + tables,
+// 3 = + rANS, 0 = complete record.
 template <int DT>
 LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restrict__ dst,
-                          EncSmem& sm) {
+                          EncSmem& sm, int stop_after = 0) {
   using S = Split16<DT>;
   constexpr int RB = DT == DT_F32 ? 3 : (DT == DT_U8 ? 0 : 1);
   constexpr int ES = DT == DT_F32 ? 4 : (DT == DT_U8 ? 1 : 2);
@@ -367,9 +369,11 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
   }
   if (RB > 0 && tid < raw_bytes - n * RB) raw_dst[n * RB + tid] = 0;
   __syncthreads();
+  if (stop_after == 1) return 0;
   // 2. frequency tables
   if (warp == 0) build_tables_warp0(sm, n);
   __syncthreads();
+  if (stop_after == 2) return 0;
   // 3. one warp per sub-block: interleaved rANS, backward over the steps
   const uint32_t nsub = (n + SUB_ELEMS - 1) / SUB_ELEMS;
   if (warp < nsub) {
@@ -415,6 +419,7 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
     if (lane == 0) sm.sub_len[warp] = overflow ? 0u : 128u + 2u * pos;
   }
   __syncthreads();
+  if (stop_after == 3) return 0;
   // 4. mode decision and record emission
   __shared__ uint32_t s_mode, s_symbytes, s_tabbytes;
   if (tid == 0) {

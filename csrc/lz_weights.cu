@@ -342,10 +342,11 @@ __global__ void __launch_bounds__(256) wx_direct_kernel(LzDevComm c, WxDirectPar
         const uint64_t off = ch * kDirectChunk;
         const uint32_t len = (uint32_t)min(kDirectChunk, d.bytes - off);
         if (p.use_mc) {
-          push_bytes<true>(c.heap_mc + d.dst_off + off, d.src + off, len);
+          push_bytes<true>(c.heap_mc + d.dst_off + off, d.src + off, len);  // every rank, sender included
         } else {
           for (int r = 0; r < W; ++r)
-            if ((p.recv_mask >> r) & 1u) push_bytes<false>(c.heap[r] + d.dst_off + off, d.src + off, len);
+            if (((p.recv_mask >> r) & 1u) || r == c.rank)
+              push_bytes<false>(c.heap[r] + d.dst_off + off, d.src + off, len);
         }
       }
     }

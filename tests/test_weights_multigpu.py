@@ -57,8 +57,16 @@ def _worker(rank, world, cases, dump_dir):
         wt.broadcast_direct(sym, 0, src_tensors=list(ref.values()) if rank == 0 else None, nblocks=32)
     torch.cuda.synchronize()
     comm.check()
-    results.append(("raw", "direct", 0.0, all(torch.equal(a.view(torch.int16), b.view(torch.int16))
-                                              for a, b in zip(sym, ref.values()))))
+    bad_idx = [i for i, (a, b) in enumerate(zip(sym, ref.values()))
+               if not torch.equal(a.view(torch.int16), b.view(torch.int16))]
+    diag = ""
+    if bad_idx:
+        a, b = sym[bad_idx[0]].view(-1).view(torch.int16), list(ref.values())[bad_idx[0]].view(-1).view(torch.int16)
+        first = int((a != b).nonzero()[0].item())
+        diag = (f"rank {rank}: {len(bad_idx)}/{len(sym)} tensors differ; first tensor {bad_idx[0]} "
+                f"numel {a.numel()} first diff at {first} got {int(a[first])} want {int(b[first])} "
+                f"ptr%16={sym[bad_idx[0]].data_ptr() % 16}")
+    results.append(("raw", "direct", diag, not bad_idx))
     # dump oracle: rank 0 dumps, the others compare what they received with it
     if rank == 0:
         weights.dump_tensors(list(ref.items()), dump_dir, 3, 0, group_name="test")
