@@ -19,7 +19,7 @@ using namespace lzg;
 namespace {
 
 template <int DT>
-__global__ void __launch_bounds__(LZC_THREADS) encode_slotted_kernel(const char* __restrict__ in,
+__global__ void __launch_bounds__(LZC_THREADS, LZC_MIN_BLOCKS) encode_slotted_kernel(const char* __restrict__ in,
                                                                       uint64_t n, char* slots,
                                                                       uint32_t slot_cap,
                                                                       uint32_t* sizes, int stop_after) {
@@ -91,7 +91,7 @@ __global__ void gather_records_kernel(const char* __restrict__ slots, uint32_t s
 }
 
 template <int DT>
-__global__ void __launch_bounds__(LZC_THREADS) decode_stream_kernel(const char* __restrict__ st,
+__global__ void __launch_bounds__(LZC_THREADS, LZC_MIN_BLOCKS) decode_stream_kernel(const char* __restrict__ st,
                                                                      uint64_t stream_bytes,
                                                                      char* __restrict__ out,
                                                                      uint64_t n, int* status) {
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(LZC_THREADS) decode_stream_kernel(const char* 
 }
 
 template <int DT>
-__global__ void __launch_bounds__(LZC_THREADS) decode_slotted_kernel(const char* __restrict__ slots,
+__global__ void __launch_bounds__(LZC_THREADS, LZC_MIN_BLOCKS) decode_slotted_kernel(const char* __restrict__ slots,
                                                                       uint32_t slot_cap,
                                                                       char* __restrict__ out,
                                                                       uint64_t n, int* status) {

@@ -13,7 +13,8 @@
 namespace lzg {
 
 using namespace lzc;
-constexpr int LZC_THREADS = 128;
+constexpr int LZC_THREADS = 256;  // one warp per sub-block
+constexpr int LZC_MIN_BLOCKS = 3;  // 3 CTAs (24 warps) per SM: caps registers at 85
 static_assert(LZC_THREADS / 32 == NSUB, "one warp per sub-block");
 
 struct EncSmem {
@@ -217,7 +218,9 @@ LZ_DEV void build_tables_warp0(EncSmem& sm, uint32_t n) {
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int s = lane * 8 + k;
-    c[k] = sm.u.counts[0][s] + sm.u.counts[1][s] + sm.u.counts[2][s] + sm.u.counts[3][s];
+    c[k] = 0;
+#pragma unroll
+    for (int w = 0; w < NSUB; ++w) c[k] += sm.u.counts[w][s];
     f[k] = 0;
     if (c[k]) {
       f[k] = (uint32_t)(((uint64_t)c[k] * PROB_SCALE) / n);

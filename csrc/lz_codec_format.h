@@ -48,9 +48,9 @@ constexpr uint32_t PROB_BITS = 11;
 constexpr uint32_t PROB_SCALE = 1u << PROB_BITS;
 constexpr uint32_t RANS_L = 1u << 16;
 constexpr int LANES = 32;
-constexpr int SUB_STEPS = 256;
-constexpr uint32_t SUB_ELEMS = LANES * SUB_STEPS;  // 8192
-constexpr int NSUB = 4;
+constexpr int SUB_STEPS = 128;
+constexpr uint32_t SUB_ELEMS = LANES * SUB_STEPS;  // 4096
+constexpr int NSUB = 8;
 constexpr uint32_t TG_ELEMS = SUB_ELEMS * NSUB;    // 32768
 constexpr uint32_t TG_MAGIC = 0x47545A4Cu;         // "LZTG"
 constexpr uint32_t STREAM_MAGIC = 0x31435A4Cu;     // "LZC1"

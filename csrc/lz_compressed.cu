@@ -208,13 +208,13 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
 }
 
 template <int DT>
-__global__ void __launch_bounds__(LZC_THREADS) cz_allreduce_kernel(LzDevComm c, CzParams p) {
+__global__ void __launch_bounds__(LZC_THREADS, LZC_MIN_BLOCKS) cz_allreduce_kernel(LzDevComm c, CzParams p) {
   cz_allreduce_body<DT>(c, p);
 }
 
 // Single-GPU emulation: block (x, y) is block x of rank y (cooperative launch).
 template <int DT>
-__global__ void __launch_bounds__(LZC_THREADS) cz_allreduce_emu_kernel(const LzDevComm* cs,
+__global__ void __launch_bounds__(LZC_THREADS, LZC_MIN_BLOCKS) cz_allreduce_emu_kernel(const LzDevComm* cs,
                                                                        const CzParams* ps) {
   cz_allreduce_body<DT>(cs[blockIdx.y], ps[blockIdx.y]);
 }

@@ -16,6 +16,8 @@
 // back_up/update_weight_from_distributed.py:422-449 and the UCCL-P2P
 // split/encode sends whose logs and CSVs the reference keeps
 // (raw/bf16_split_sm16_split_encode_time_count.txt, csv/weight_update_rl_GLM4_9B.csv).
+#include <stdlib.h>
+
 #include "lz_codec_dev.cuh"
 #include "lz_internal.h"
 
@@ -46,6 +48,7 @@ struct WxParams {
   uint32_t recv_mask;
   int use_mc;
   int kslots;
+  int group;         // table groups per work item (one flag round trip per item)
   uint32_t cap;
   size_t slots_off;
   size_t ready_off;
@@ -147,10 +150,12 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
 
   if (p.role == 0) {
     // ---------------------------------------------------------------- sender
-    for (uint32_t i = 0; b + (uint64_t)i * G < p.ntg; ++i) {
-      const uint32_t t = b + i * G;
+    // item i of CTA b = table groups [(b + i*G) * g, (b + i*G) * g + g)
+    const uint32_t g = (uint32_t)p.group;
+    const uint32_t nitems = (p.ntg + g - 1) / g;
+    for (uint32_t i = 0; b + (uint64_t)i * G < nitems; ++i) {
+      const uint32_t item = b + i * G;
       const uint32_t k = i % K;
-      const WxDesc d = p.descs[t];
       const int t_r = threadIdx.x;
       if (i >= (uint32_t)K && t_r < W && ((p.recv_mask >> t_r) & 1u)) {
         const unsigned long long* cr = reinterpret_cast<const unsigned long long*>(
@@ -159,26 +164,29 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
       }
       __syncthreads();
       if (s_fail) return;
-      const size_t slot_off = p.slots_off + ((size_t)b * K + k) * p.cap;
-      char* local = c.heap[me] + slot_off;
-      const int es = es_of(d.dtype);
-      if (d.encode) {
-        const bool direct = !p.use_mc && nrecv == 1;
-        char* dst = direct ? c.heap[only] + slot_off : local;
-        const uint32_t bytes = encode_dispatch(d.dtype, d.ptr, d.n, dst, sm.enc);
-        if (p.use_mc) {
-          push_bytes<true>(c.heap_mc + slot_off, local, pad16(bytes));
-        } else if (!direct) {
-          for (int r = 0; r < W; ++r)
-            if ((p.recv_mask >> r) & 1u) push_bytes<false>(c.heap[r] + slot_off, local, pad16(bytes));
-        }
-      } else {
-        const uint32_t bytes = d.n * (uint32_t)es;
-        if (p.use_mc) {
-          push_bytes<true>(c.heap_mc + slot_off, d.ptr, bytes);
+      for (uint32_t j = 0; j < g && item * g + j < p.ntg; ++j) {
+        const WxDesc d = p.descs[item * g + j];
+        const size_t slot_off = p.slots_off + (((size_t)b * K + k) * g + j) * p.cap;
+        char* local = c.heap[me] + slot_off;
+        const int es = es_of(d.dtype);
+        if (d.encode) {
+          const bool direct = !p.use_mc && nrecv == 1;
+          char* dst = direct ? c.heap[only] + slot_off : local;
+          const uint32_t bytes = encode_dispatch(d.dtype, d.ptr, d.n, dst, sm.enc);
+          if (p.use_mc) {
+            push_bytes<true>(c.heap_mc + slot_off, local, pad16(bytes));
+          } else if (!direct) {
+            for (int r = 0; r < W; ++r)
+              if ((p.recv_mask >> r) & 1u) push_bytes<false>(c.heap[r] + slot_off, local, pad16(bytes));
+          }
         } else {
-          for (int r = 0; r < W; ++r)
-            if ((p.recv_mask >> r) & 1u) push_bytes<false>(c.heap[r] + slot_off, d.ptr, bytes);
+          const uint32_t bytes = d.n * (uint32_t)es;
+          if (p.use_mc) {
+            push_bytes<true>(c.heap_mc + slot_off, d.ptr, bytes);
+          } else {
+            for (int r = 0; r < W; ++r)
+              if ((p.recv_mask >> r) & 1u) push_bytes<false>(c.heap[r] + slot_off, d.ptr, bytes);
+          }
         }
       }
       __syncthreads();
@@ -202,35 +210,39 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
         c.heap[me] + p.ready_off) + (size_t)p.src * LZ_MAX_BLOCKS + b;
     unsigned long long* credit = reinterpret_cast<unsigned long long*>(c.heap[p.src] + p.credit_off) +
                                  (size_t)b * LZ_MAX_RANKS + me;
-    for (uint32_t i = 0; b + (uint64_t)i * G < p.ntg; ++i) {
-      const uint32_t t = b + i * G;
+    const uint32_t g = (uint32_t)p.group;
+    const uint32_t nitems = (p.ntg + g - 1) / g;
+    for (uint32_t i = 0; b + (uint64_t)i * G < nitems; ++i) {
+      const uint32_t item = b + i * G;
       const uint32_t k = i % K;
-      const WxDesc d = p.descs[t];
       if (threadIdx.x == 0 && !lz_wait_ge(c, ready, p.seq[0] | (unsigned long long)(i + 1), 6, p.src))
         s_fail = 1;
       __syncthreads();
       if (s_fail) return;
       if (threadIdx.x == 0 && p.use_mc) fence_proxy_alias();
       __syncthreads();
-      const char* slot = c.heap[me] + p.slots_off + ((size_t)b * K + k) * p.cap;
-      if (d.encode) {
-        if (!decode_dispatch(d.dtype, slot, p.cap, d.n, d.ptr, sm.dec)) {
-          if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 7, p.src);
-          return;
-        }
-      } else {
-        const uint32_t bytes = d.n * (uint32_t)es_of(d.dtype);
-        const uint32_t full = bytes & ~15u;
-        uint32_t o = threadIdx.x * 16;
-        for (; o + 3 * blockDim.x * 16 < full; o += 4 * blockDim.x * 16) {
-          uint4 v[4];
+      for (uint32_t j = 0; j < g && item * g + j < p.ntg; ++j) {
+        const WxDesc d = p.descs[item * g + j];
+        const char* slot = c.heap[me] + p.slots_off + (((size_t)b * K + k) * g + j) * p.cap;
+        if (d.encode) {
+          if (!decode_dispatch(d.dtype, slot, p.cap, d.n, d.ptr, sm.dec)) {
+            if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 7, p.src);
+            return;
+          }
+        } else {
+          const uint32_t bytes = d.n * (uint32_t)es_of(d.dtype);
+          const uint32_t full = bytes & ~15u;
+          uint32_t o = threadIdx.x * 16;
+          for (; o + 3 * blockDim.x * 16 < full; o += 4 * blockDim.x * 16) {
+            uint4 v[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) v[u] = ld_cg_v4(slot + o + u * blockDim.x * 16);
+            for (int u = 0; u < 4; ++u) v[u] = ld_cg_v4(slot + o + u * blockDim.x * 16);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) st_v4(d.ptr + o + u * blockDim.x * 16, v[u]);
+            for (int u = 0; u < 4; ++u) st_v4(d.ptr + o + u * blockDim.x * 16, v[u]);
+          }
+          for (; o < full; o += blockDim.x * 16) st_v4(d.ptr + o, ld_cg_v4(slot + o));
+          if (threadIdx.x < bytes - full) d.ptr[full + threadIdx.x] = (char)ld_cg_u8(slot + full + threadIdx.x);
         }
-        for (; o < full; o += blockDim.x * 16) st_v4(d.ptr + o, ld_cg_v4(slot + o));
-        if (threadIdx.x < bytes - full) d.ptr[full + threadIdx.x] = (char)ld_cg_u8(slot + full + threadIdx.x);
       }
       __syncthreads();
       if (threadIdx.x == 0) {
@@ -241,7 +253,7 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
   }
 }
 
-__global__ void __launch_bounds__(LZC_THREADS) wx_kernel(LzDevComm c, WxParams p) { wx_body(c, p); }
+__global__ void __launch_bounds__(LZC_THREADS, 2) wx_kernel(LzDevComm c, WxParams p) { wx_body(c, p); }
 
 }  // namespace
 
@@ -252,6 +264,14 @@ extern "C" size_t lz_wx_tg_elems(void) { return TG_ELEMS; }
 extern "C" size_t lz_wx_stage_bytes(int nblocks, int kslots) {
   return (size_t)nblocks * kslots * tg_capacity(LZ_F32);
 }
+
+// Table groups per work item used by lz_weight_transfer (env LZ_WX_GROUP, default 4).
+static int wx_group() {
+  const char* e = getenv("LZ_WX_GROUP");
+  const int g = e ? atoi(e) : 4;
+  return g < 1 ? 1 : (g > 16 ? 16 : g);
+}
+extern "C" int lz_wx_group(void) { return wx_group(); }
 
 // role 0 = sender (seq[r] per receiver r), 1 = receiver (seq[0]).
 // descs: device array of 16-byte descriptors (ptr, n, dtype, encode).
@@ -281,9 +301,10 @@ extern "C" int lz_weight_transfer(LzComm* c, int role, int src, unsigned int rec
   p.kslots = kslots;
   p.cap = tg_capacity(LZ_F32);
   p.slots_off = c->stage_off;
-  if (lz_wx_stage_bytes(G, kslots) > c->stage_bytes) {
-    lz_set_error("weight transfer: %d blocks x %d slots need %zu stage bytes, have %zu", G, kslots,
-                 lz_wx_stage_bytes(G, kslots), c->stage_bytes);
+  p.group = wx_group();
+  if (lz_wx_stage_bytes(G, kslots) * p.group > c->stage_bytes) {
+    lz_set_error("weight transfer: %d blocks x %d slots x %d groups need %zu stage bytes, have %zu", G,
+                 kslots, p.group, lz_wx_stage_bytes(G, kslots) * p.group, c->stage_bytes);
     return LZE_ARG;
   }
   p.ready_off = all ? kReadyB : kReadyP;
@@ -324,6 +345,7 @@ struct WxDirectParams {
   uint32_t recv_mask;
   int use_mc;
   size_t ready_off;
+  size_t credit_off;
   unsigned long long seq[LZ_MAX_RANKS];
 };
 
@@ -332,6 +354,18 @@ constexpr uint64_t kDirectChunk = 256u << 10;  // bytes per work item
 __global__ void __launch_bounds__(256) wx_direct_kernel(LzDevComm c, WxDirectParams p) {
   const int W = c.world, G = gridDim.x, b = blockIdx.x;
   if (p.role == 0) {
+    // every receiver's CTA b must have started (its earlier work on the
+    // destination tensors is done, stream order) before CTA b writes
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) s_fail = 0;
+    __syncthreads();
+    if (threadIdx.x < W && ((p.recv_mask >> threadIdx.x) & 1u)) {
+      const unsigned long long* cr = reinterpret_cast<const unsigned long long*>(c.heap[c.rank] + p.credit_off) +
+                                     (size_t)b * LZ_MAX_RANKS + threadIdx.x;
+      if (!lz_wait_ge(c, cr, p.seq[threadIdx.x] | 1ull, 10, threadIdx.x)) s_fail = 1;
+    }
+    __syncthreads();
+    if (s_fail) return;
     // work items: 256 KB chunks of every descriptor, dealt round-robin to CTAs
     uint64_t item = 0;
     for (uint32_t k = 0; k < p.ndesc; ++k) {
@@ -360,6 +394,10 @@ __global__ void __launch_bounds__(256) wx_direct_kernel(LzDevComm c, WxDirectPar
     }
   } else {
     if (threadIdx.x == 0) {
+      unsigned long long* cr = reinterpret_cast<unsigned long long*>(c.heap[p.src] + p.credit_off) +
+                               (size_t)b * LZ_MAX_RANKS + c.rank;
+      fence_sys();
+      st_release_sys(cr, p.seq[0] | 1ull);  // clear to send
       const unsigned long long* f = reinterpret_cast<const unsigned long long*>(c.heap[c.rank] + p.ready_off) +
                                     (size_t)p.src * LZ_MAX_BLOCKS + b;
       lz_wait_ge(c, f, p.seq[0] | 1ull, 8, p.src);
@@ -392,6 +430,7 @@ extern "C" int lz_weight_transfer_direct(LzComm* c, int role, int src, unsigned 
   const bool all = broadcast_all && recv_mask == (((1u << W) - 1u) & ~(1u << src));
   p.use_mc = (all && W > 2 && c->dev.heap_mc) ? 1 : 0;
   p.ready_off = all ? kReadyB : kReadyP;
+  p.credit_off = all ? kCreditB : kCreditP;
   for (int r = 0; r < LZ_MAX_RANKS; ++r) p.seq[r] = seqs[r] << 32;
   wx_direct_kernel<<<G, 256, 0, s>>>(c->dev, p);
   LZ_CUDA_TRY(cudaGetLastError());

@@ -37,6 +37,7 @@ _native_sigs.add_cuda({
     "lz_wx_slot_capacity": (C.c_size_t,),
     "lz_wx_tg_elems": (C.c_size_t,),
     "lz_wx_stage_bytes": (C.c_size_t, C.c_int, C.c_int),
+    "lz_wx_group": (C.c_int,),
     "lz_weight_transfer": (C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_uint, C.c_void_p, C.c_uint, C.c_int,
                            C.c_int, C.c_int, C.POINTER(C.c_uint64), C.c_void_p),
     "lz_weight_transfer_direct": (C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_uint, C.c_void_p, C.c_uint,
@@ -87,7 +88,7 @@ class WeightTransfer:
         self.comm = comm
         self.mode = mode
         self.encode_fraction = encode_fraction if mode == "split_ans" else 0.0
-        self.nblocks = nblocks or min(comm.sm_count * 3, 512)
+        self.nblocks = nblocks or comm.sm_count * 2
         cap_tg_bytes = TG * 2
         if kslots:
             self.kslots = kslots
@@ -96,9 +97,12 @@ class WeightTransfer:
         else:
             self.kslots = 4
         lib = comm._lib
-        need = lib.lz_wx_stage_bytes(self.nblocks, self.kslots)
+        grp = lib.lz_wx_group()
+        need = lib.lz_wx_stage_bytes(self.nblocks, self.kslots) * grp
         if need > comm.config.stage_bytes:
-            self.kslots = max(2, comm.config.stage_bytes // (self.nblocks * lib.lz_wx_slot_capacity()))
+            self.kslots = max(2, comm.config.stage_bytes // (self.nblocks * lib.lz_wx_slot_capacity() * grp))
+            if lib.lz_wx_stage_bytes(self.nblocks, self.kslots) * grp > comm.config.stage_bytes:
+                self.nblocks = max(1, comm.config.stage_bytes // (2 * lib.lz_wx_slot_capacity() * grp))
         # Flag sequence numbers must be monotonic per communicator (not per
         # engine): every engine on `comm` shares the same flag words.
         if not hasattr(comm, "_wx_pair_seq"):

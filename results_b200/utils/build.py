@@ -73,7 +73,7 @@ def cpu_sources() -> list[Path]:
 
 def build_cpu(force: bool = False) -> Path:
     srcs = cpu_sources()
-    hdrs = sorted((CSRC / "cpu").glob("*.h"))
+    hdrs = sorted((CSRC / "cpu").glob("*.h")) + [CSRC / "lz_codec_format.h"]
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     if not force and CPU_LIB.exists() and CPU_LIB.stat().st_mtime >= _newest(srcs + hdrs):
         return CPU_LIB
