@@ -15,14 +15,16 @@ namespace lzg {
 using namespace lzc;
 constexpr int LZC_THREADS = 256;  // one warp per sub-block
 constexpr int LZC_MIN_BLOCKS = 3;  // 3 CTAs (24 warps) per SM: caps registers at 85
+constexpr int HREP = 4;            // histogram replicas per warp (lane & 3)
 static_assert(LZC_THREADS / 32 == NSUB, "one warp per sub-block");
 
 struct EncSmem {
   uint8_t syms[TG_ELEMS];  // symbol plane of the TG
   union {
-    uint8_t streams[NSUB][SUB_ELEMS];  // per-warp rANS output (states + words)
-    uint32_t counts[NSUB][256];        // per-warp histograms (before encoding)
+    uint8_t streams[NSUB][SUB_ELEMS];     // per-warp rANS output (states + words)
+    uint32_t counts[NSUB][HREP][256];     // per-warp histograms, HREP replicas (before encoding)
   } u;
+  uint32_t hist[256];                     // reduced histogram
   EncSym tab[256];
   uint32_t table[256];
   uint32_t sub_len[NSUB];
@@ -218,9 +220,7 @@ LZ_DEV void build_tables_warp0(EncSmem& sm, uint32_t n) {
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int s = lane * 8 + k;
-    c[k] = 0;
-#pragma unroll
-    for (int w = 0; w < NSUB; ++w) c[k] += sm.u.counts[w][s];
+    c[k] = sm.hist[s];
     f[k] = 0;
     if (c[k]) {
       f[k] = (uint32_t)(((uint64_t)c[k] * PROB_SCALE) / n);
@@ -320,7 +320,7 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
   const uint32_t raw_bytes = pad16(n * RB);
   char* raw_dst = dst + sizeof(TgHeader);
 
-  for (uint32_t k = tid; k < NSUB * 256; k += blockDim.x) (&sm.u.counts[0][0])[k] = 0;
+  for (uint32_t k = tid; k < NSUB * HREP * 256; k += blockDim.x) (&sm.u.counts[0][0][0])[k] = 0;
   __syncthreads();
   // 1. split + histogram (+ raw plane straight to the destination)
   const uint32_t units = n / 16;
@@ -353,12 +353,12 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
           st_v4(raw_dst + (size_t)u * S::RAW_BYTES + 16 * q, reinterpret_cast<const uint4*>(rw)[q]);
       }
     }
-    // warp-aggregated histogram: one shared atomic per distinct symbol
+    // replicated per-warp histograms: one shared atomic per symbol, lanes
+    // spread over HREP copies to cut same-address serialisation
+    if (act) {
+      uint32_t* h = sm.u.counts[warp][lane & (HREP - 1)];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const uint32_t key = act ? (uint32_t)sy[k] : 256u + lane;
-      const uint32_t peers = __match_any_sync(0xffffffffu, key);
-      if (act && (__ffs(peers) - 1) == (int)lane) atomicAdd(&sm.u.counts[warp][sy[k]], __popc(peers));
+      for (int k = 0; k < 16; ++k) atomicAdd(&h[sy[k]], 1u);
     }
   }
   // tail elements (n % 16) and the zero padding of the raw plane
@@ -367,13 +367,22 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
     uint8_t s1, r1[4];
     split1<DT>(in, i, &s1, r1);
     sm.syms[i] = s1;
-    atomicAdd(&sm.u.counts[0][s1], 1u);
+    atomicAdd(&sm.u.counts[0][0][s1], 1u);
     for (int q = 0; q < RB; ++q) raw_dst[(size_t)i * RB + q] = (char)r1[q];
   }
   if (RB > 0 && tid < raw_bytes - n * RB) raw_dst[n * RB + tid] = 0;
   __syncthreads();
   if (stop_after == 1) return 0;
-  // 2. frequency tables
+  // 2. frequency tables: reduce the replicas (one bin per thread), then warp 0
+  for (uint32_t sbin = tid; sbin < 256; sbin += blockDim.x) {
+    uint32_t c = 0;
+#pragma unroll
+    for (int w = 0; w < NSUB; ++w)
+#pragma unroll
+      for (int r = 0; r < HREP; ++r) c += sm.u.counts[w][r][sbin];
+    sm.hist[sbin] = c;
+  }
+  __syncthreads();
   if (warp == 0) build_tables_warp0(sm, n);
   __syncthreads();
   if (stop_after == 2) return 0;
