@@ -275,11 +275,10 @@ extern "C" int lz_wx_group(void) { return wx_group(); }
 
 // role 0 = sender (seq[r] per receiver r), 1 = receiver (seq[0]).
 // descs: device array of 16-byte descriptors (ptr, n, dtype, encode).
-extern "C" int lz_weight_transfer(LzComm* c, int role, int src, unsigned int recv_mask,
-                                  const void* descs, unsigned int ntg, int nblocks, int kslots,
-                                  int broadcast_all, const unsigned long long* seqs, cudaStream_t s) {
+static int wx_plan(const LzComm* c, int role, int src, unsigned int recv_mask, const void* descs,
+                   unsigned int ntg, int nblocks, int kslots, int broadcast_all,
+                   const unsigned long long* seqs, WxParams* out, int* grid) {
   const int W = c->dev.world;
-  if (W == 1 || ntg == 0) return LZE_OK;
   if (src < 0 || src >= W || (recv_mask >> src) & 1u || recv_mask == 0 ||
       (recv_mask >> W) != 0u) {
     lz_set_error("weight transfer: bad src %d / receiver mask 0x%x", src, recv_mask);
@@ -310,11 +309,67 @@ extern "C" int lz_weight_transfer(LzComm* c, int role, int src, unsigned int rec
   p.ready_off = all ? kReadyB : kReadyP;
   p.credit_off = all ? kCreditB : kCreditP;
   for (int r = 0; r < LZ_MAX_RANKS; ++r) p.seq[r] = seqs[r] << 32;
+  *out = p;
+  *grid = G;
+  return LZE_OK;
+}
+
+extern "C" int lz_weight_transfer(LzComm* c, int role, int src, unsigned int recv_mask,
+                                  const void* descs, unsigned int ntg, int nblocks, int kslots,
+                                  int broadcast_all, const unsigned long long* seqs, cudaStream_t s) {
+  if (c->dev.world == 1 || ntg == 0) return LZE_OK;
+  WxParams p;
+  int G = 0;
+  int rc = wx_plan(c, role, src, recv_mask, descs, ntg, nblocks, kslots, broadcast_all, seqs, &p, &G);
+  if (rc) return rc;
   const size_t smem = sizeof(WxSmem);
   void* fn = reinterpret_cast<void*>(&wx_kernel);
   LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* args[] = {&c->dev, &p};
   LZ_CUDA_TRY(cudaLaunchKernel(fn, dim3(G), dim3(LZC_THREADS), args, smem, s));
+  return LZE_OK;
+}
+
+// Single-GPU emulation of one transfer: block (x, y) is CTA x of emulated
+// rank y, all in ONE cooperative launch; ranks that neither send nor receive
+// idle. descs[r]: device descriptor table of rank r; seqs: R x 8 values.
+namespace {
+__global__ void __launch_bounds__(LZC_THREADS, 2) wx_emu_kernel(const LzDevComm* cs, const WxParams* ps) {
+  const WxParams& p = ps[blockIdx.y];
+  if (p.role > 1) return;
+  wx_body(cs[blockIdx.y], p);
+}
+}  // namespace
+
+extern "C" int lz_emu_weight_transfer(LzEmu* e, int src, unsigned int recv_mask, const void* const* descs,
+                                      unsigned int ntg, int nblocks, int kslots, int broadcast_all,
+                                      const unsigned long long* seqs, cudaStream_t s) {
+  const int R = lz_emu_world(e);
+  WxParams hp[LZ_MAX_RANKS];
+  int G = 0;
+  for (int r = 0; r < R; ++r) {
+    const int role = r == src ? 0 : (((recv_mask >> r) & 1u) ? 1 : 2);
+    int rc = wx_plan(lz_emu_comm(e, r), role < 2 ? role : 1, src, recv_mask, descs[r], ntg, nblocks, kslots,
+                     broadcast_all, seqs + 8 * r, &hp[r], &G);
+    if (rc) return rc;
+    hp[r].role = role;
+  }
+  const size_t smem = sizeof(WxSmem);
+  void* fn = reinterpret_cast<void*>(&wx_emu_kernel);
+  LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  LZ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, LZC_THREADS, smem));
+  if ((long long)G * R > (long long)per_sm * lz_emu_comm(e, 0)->sm_count) {
+    lz_set_error("emulated weight transfer: %d x %d blocks exceed co-residency", G, R);
+    return LZE_ARG;
+  }
+  static_assert(sizeof(WxParams) * LZ_MAX_RANKS <= 4096, "param buffer");
+  void* dparams = lz_emu_param_buffer(e);
+  LZ_CUDA_TRY(cudaMemcpyAsync(dparams, hp, sizeof(WxParams) * R, cudaMemcpyHostToDevice, s));
+  LzDevComm* dcomms = lz_emu_dev_comms(e);
+  void* args[] = {&dcomms, &dparams};
+  LZ_CUDA_TRY(cudaLaunchCooperativeKernel(fn, dim3(G, R), dim3(LZC_THREADS), args, smem, s));
+  LZ_CUDA_TRY(cudaStreamSynchronize(s));
   return LZE_OK;
 }
 

@@ -73,6 +73,45 @@ class EmulatedWorld:
                                                    torch.cuda.current_stream().cuda_stream)
         _native.check(rc, "emulated compressed allreduce")
 
+    def weight_transfer(self, src: int, dsts, tensors, encode: bool = True, nblocks: int = 16,
+                        kslots: int = 3, broadcast_all: bool = False):
+        """One transfer from emulated rank `src` to `dsts`; tensors[r] is rank r's list."""
+        from . import weights
+
+        R = self.world
+        if not hasattr(self, "_wx_seq"):
+            self._wx_seq = {}
+        mask = 0
+        for d in dsts:
+            mask |= 1 << d
+        seqs = [0] * (8 * R)
+        for d in dsts:
+            key = ("b", src) if broadcast_all else (src, d)
+            k = self._wx_seq.get(key, 0) + (0 if broadcast_all and d != dsts[0] else 1)
+            self._wx_seq[key] = k
+        for r in range(R):
+            for q in range(8):
+                if broadcast_all:
+                    seqs[8 * r + q] = self._wx_seq[("b", src)]
+                elif r == src:
+                    seqs[8 * r + q] = self._wx_seq.get((src, q), 0) if q in dsts else 0
+                elif r in dsts:
+                    seqs[8 * r + q] = self._wx_seq[(src, r)]
+        keep = []
+        ptrs = []
+        ntg = None
+        for r in range(R):
+            ts = tensors[r] if tensors[r] is not None else tensors[src]
+            d, n = weights.build_descriptors(ts, [encode] * len(ts), f"cuda:{self.device}")
+            keep.append(d)
+            ptrs.append(d.data_ptr())
+            ntg = n
+        arr = (C.c_void_p * R)(*ptrs)
+        sq = (C.c_uint64 * (8 * R))(*seqs)
+        rc = self._lib.lz_emu_weight_transfer(self._emu, src, mask, arr, ntg, nblocks, kslots,
+                                              int(broadcast_all), sq, torch.cuda.current_stream().cuda_stream)
+        _native.check(rc, "emulated weight transfer")
+
     def status(self, r: int) -> int:
         return self._lib.lz_emu_status(self._emu, r)
 

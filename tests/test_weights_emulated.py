@@ -1,0 +1,46 @@
+"""Weight-transfer kernel (K-slot credit pipeline, grouped work items,
+split+rANS or raw) with sender and receivers emulated on ONE GPU in one
+cooperative launch. Repeated transfers of changing data catch stale-slot
+reads; receivers must end bit-identical to the sender."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def world3():
+    from results_b200.parallel.emulate import EmulatedWorld
+
+    w = EmulatedWorld(3, heap_bytes=(640 << 20), stage_bytes=(512 << 20))
+    yield w
+    w.close()
+
+
+def _tensors(seed, device="cuda"):
+    g = torch.Generator(device=device).manual_seed(seed)
+    shapes = [(1000, 512), (512,), (3, 32768), (77, 129), (70000,)]
+    out = [(torch.randn(s, device=device, generator=g) * 0.02).to(torch.bfloat16) for s in shapes]
+    out.append((torch.randn(50000, device=device, generator=g)).to(torch.float32))
+    out.append((torch.randn(40000, device=device, generator=g) * 0.5).to(torch.float8_e4m3fn))
+    return out
+
+
+@pytest.mark.parametrize("encode", [True, False])
+@pytest.mark.parametrize("bcast", [False, True])
+def test_emulated_transfer_repeated(world3, encode, bcast):
+    R = 3
+    for it in range(4):
+        src_t = _tensors(100 * it + int(encode) + 2 * int(bcast))
+        recv = {r: [torch.full_like(t, 0) for t in src_t] for r in (1, 2)}
+        tensors = [src_t, recv[1], recv[2]]
+        if bcast:
+            world3.weight_transfer(0, [1, 2], tensors, encode=encode, broadcast_all=True)
+        else:
+            for d in (1, 2):
+                world3.weight_transfer(0, [d], tensors, encode=encode)
+        torch.cuda.synchronize()
+        for r in (1, 2):
+            assert world3.status(r) == 0
+            for a, b in zip(recv[r], src_t):
+                assert torch.equal(a.view(torch.uint8), b.view(torch.uint8)), (it, r, a.shape)
