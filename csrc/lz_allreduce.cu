@@ -406,7 +406,7 @@ __device__ __forceinline__ void ring_body(const LzDevComm& c, const ArParams& P)
         }
         if (k < hops) st_v4(right_slots + sslot * tile_vecs + i, data);
       }
-      __syncthreads();
+      publish_block_writes();
       if (threadIdx.x == 0) {
         fence_sys();
         if (k > 0) st_release_sys(left_credit, base + q_recv + 1);

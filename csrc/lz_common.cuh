@@ -255,14 +255,23 @@ LZ_DEV unsigned long long* peer_flags(const LzDevComm& c, int peer) {
   return reinterpret_cast<unsigned long long*>(c.heap[peer] + c.flags_off);
 }
 
+// Every thread fences its own peer/multicast writes at system scope before
+// the CTA barrier: a fence covers the issuing warp's outstanding stores, so a
+// single signalling thread's fence is not enough to publish the stores of the
+// other warps that are still in flight on NVLink.
+LZ_DEV void publish_block_writes() {
+  fence_sys();
+  __syncthreads();
+}
+
 // All-pairs barrier between block `blockIdx.x` of every rank. Threads
 // 0..world-1 each own one peer. Prior stores of the whole block are released
-// (bar.sync + fence.acq_rel.sys + st.release.sys is cumulative).
+// (every thread fences, bar.sync, then release stores).
 // Returns false (uniformly for the block) if a wait gave up.
 LZ_DEV bool block_barrier(const LzDevComm& c, unsigned long long epoch, int phase) {
   __shared__ int s_fail;
   if (threadIdx.x == 0) s_fail = 0;
-  __syncthreads();
+  publish_block_writes();
   const int t = threadIdx.x;
   if (t < c.world && t != c.rank) {
     const unsigned long long v = flag_value(epoch, phase);
@@ -278,7 +287,7 @@ LZ_DEV bool block_barrier(const LzDevComm& c, unsigned long long epoch, int phas
 LZ_DEV bool pair_barrier(const LzDevComm& c, unsigned long long epoch, int phase, int partner) {
   __shared__ int s_fail2;
   if (threadIdx.x == 0) s_fail2 = 0;
-  __syncthreads();
+  publish_block_writes();
   if (threadIdx.x == 0) {
     const unsigned long long v = flag_value(epoch, phase);
     fence_sys();
@@ -294,7 +303,7 @@ LZ_DEV bool pair_barrier(const LzDevComm& c, unsigned long long epoch, int phase
 LZ_DEV bool block_barrier_mc(const LzDevComm& c, unsigned long long epoch, int phase) {
   __shared__ int s_fail3;
   if (threadIdx.x == 0) s_fail3 = 0;
-  __syncthreads();
+  publish_block_writes();
   const unsigned long long v = flag_value(epoch, phase);
   if (threadIdx.x == 0) {
     fence_sys();

@@ -157,10 +157,14 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
       const uint32_t item = b + i * G;
       const uint32_t k = i % K;
       const int t_r = threadIdx.x;
-      if (i >= (uint32_t)K && t_r < W && ((p.recv_mask >> t_r) & 1u)) {
+      // first K items: the receiver's CTA b has started this transfer (so its
+      // previous transfer, stream-ordered before it, no longer reads any
+      // slot); later items: slot k was drained K items ago
+      if (t_r < W && ((p.recv_mask >> t_r) & 1u)) {
         const unsigned long long* cr = reinterpret_cast<const unsigned long long*>(
             c.heap[me] + p.credit_off) + (size_t)b * LZ_MAX_RANKS + t_r;
-        if (!lz_wait_ge(c, cr, p.seq[t_r] | (unsigned long long)(i - K + 1), 5, t_r)) s_fail = 1;
+        const unsigned long long need = p.seq[t_r] | (i >= (uint32_t)K ? (unsigned long long)(i - K + 1) : 0ull);
+        if (!lz_wait_ge(c, cr, need, 5, t_r)) s_fail = 1;
       }
       __syncthreads();
       if (s_fail) return;
@@ -189,7 +193,7 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
           }
         }
       }
-      __syncthreads();
+      publish_block_writes();
       if (p.use_mc) {
         if (threadIdx.x == 0) {
           fence_sys();
@@ -212,6 +216,10 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
                                  (size_t)b * LZ_MAX_RANKS + me;
     const uint32_t g = (uint32_t)p.group;
     const uint32_t nitems = (p.ntg + g - 1) / g;
+    if (threadIdx.x == 0 && b < nitems) {
+      fence_sys();
+      st_release_sys(credit, p.seq[0]);  // started: the sender may fill the slots
+    }
     for (uint32_t i = 0; b + (uint64_t)i * G < nitems; ++i) {
       const uint32_t item = b + i * G;
       const uint32_t k = i % K;
@@ -439,7 +447,7 @@ __global__ void __launch_bounds__(256) wx_direct_kernel(LzDevComm c, WxDirectPar
         }
       }
     }
-    __syncthreads();
+    publish_block_writes();
     const int t = threadIdx.x;
     if (t < W && ((p.recv_mask >> t) & 1u)) {
       fence_sys();
