@@ -499,3 +499,188 @@ extern "C" int lz_weight_transfer_direct(LzComm* c, int role, int src, unsigned 
   LZ_CUDA_TRY(cudaGetLastError());
   return LZE_OK;
 }
+
+// ----------------------------------------------------------------------------
+// Relay broadcast into symmetric destinations (every other rank receives).
+// A broadcast is bound by each receiver's NVLink ingress (every receiver must
+// take in all the bytes), not by the sender's egress, so the sender should not
+// be the only GPU that sends. The bytes are cut into 256 KB chunks, dealt to
+// CTAs round-robin; round t of CTA b is owned by rank (b + t) % W. The sender
+// multicasts the chunks it owns itself; a chunk owned by rank o goes to o
+// alone with peer stores, and o then forwards it from its own copy to every
+// other rank (one multimem.st through the switch, or peer stores). Every
+// rank's egress is then ~1/W of the bytes (the sender's ~all of them once),
+// and every receiver takes in each byte once.
+// CTA b of all ranks meets in an all-pairs barrier before its first store
+// (every rank has started, so earlier stream work on the destinations is
+// done) and after its last one (every chunk of CTA b has landed everywhere).
+// Flags live in per-sender regions so calls from different senders never mix.
+// ----------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kRelayBar = 196608;           // [src] x [block][rank] u64 barrier flags
+constexpr size_t kRelayBarStride = 32768;
+constexpr size_t kRelayReady = 458752;          // [src] x [block] u64 chunk-ready flags (owner's heap)
+constexpr size_t kRelayReadyStride = 4096;
+static_assert(kRelayBar + LZ_MAX_RANKS * kRelayBarStride <= kRelayReady, "relay flag regions overlap");
+static_assert(kRelayReady + LZ_MAX_RANKS * kRelayReadyStride <= (512u << 10), "relay flags reach the test word");
+
+struct WxRelayParams {
+  const WxDirectDesc* descs;
+  uint32_t ndesc;
+  int src;
+  int use_mc;
+  unsigned long long seq;  // sequence << 32
+};
+
+// All-pairs meeting of CTA b of every rank at value v (per-sender region).
+LZ_DEV bool relay_barrier(const LzDevComm& c, size_t bar_off, unsigned long long v, int phase) {
+  __shared__ int s_fail_rb;
+  if (threadIdx.x == 0) s_fail_rb = 0;
+  publish_block_writes();
+  const int t = threadIdx.x;
+  if (t < c.world && t != c.rank) {
+    unsigned long long* mine = reinterpret_cast<unsigned long long*>(c.heap[t] + bar_off) +
+                               (size_t)blockIdx.x * LZ_MAX_RANKS + c.rank;
+    fence_sys();
+    st_release_sys(mine, v);
+    const unsigned long long* theirs = reinterpret_cast<const unsigned long long*>(c.heap[c.rank] + bar_off) +
+                                       (size_t)blockIdx.x * LZ_MAX_RANKS + t;
+    if (!lz_wait_ge(c, theirs, v, phase, t)) s_fail_rb = 1;
+  }
+  __syncthreads();
+  return s_fail_rb == 0;
+}
+
+// Peer stores of `len` bytes at heap offset `off` to every rank but `skip`
+// (and but this rank when `src` is this rank's own copy).
+LZ_DEV void relay_push_p2p(const LzDevComm& c, uint64_t off, const char* src, uint32_t len, int skip) {
+  for (int r = 0; r < c.world; ++r) {
+    if (r == skip) continue;
+    char* dst = c.heap[r] + off;
+    if (dst == src) continue;
+    push_bytes<false>(dst, src, len);
+  }
+}
+
+__device__ __forceinline__ void wx_relay_body(const LzDevComm& c, const WxRelayParams& p) {
+  const int W = c.world, me = c.rank, G = gridDim.x, b = blockIdx.x;
+  const size_t bar_off = kRelayBar + (size_t)p.src * kRelayBarStride;
+  const size_t rdy_off = kRelayReady + (size_t)p.src * kRelayReadyStride;
+  if (!relay_barrier(c, bar_off, p.seq | 1ull, 11)) return;
+  __shared__ int s_fail;
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  uint64_t item = 0;
+  uint32_t t = 0;  // round of this CTA
+  for (uint32_t k = 0; k < p.ndesc; ++k) {
+    const WxDirectDesc d = p.descs[k];
+    const uint64_t nchunks = (d.bytes + kDirectChunk - 1) / kDirectChunk;
+    for (uint64_t ch = 0; ch < nchunks; ++ch, ++item) {
+      if (item % G != (uint64_t)b) continue;
+      const uint32_t round = t++;
+      const int owner = (int)((b + round) % (uint32_t)W);
+      const uint64_t off = ch * kDirectChunk;
+      const uint32_t len = (uint32_t)min(kDirectChunk, d.bytes - off);
+      const uint64_t hoff = d.dst_off + off;
+      if (me == p.src) {
+        if (owner == me) {
+          if (p.use_mc) push_bytes<true>(c.heap_mc + hoff, d.src + off, len);
+          else relay_push_p2p(c, hoff, d.src + off, len, -1);
+        } else {
+          push_bytes<false>(c.heap[owner] + hoff, d.src + off, len);
+          publish_block_writes();
+          if (threadIdx.x == 0) {
+            fence_sys();
+            unsigned long long* f = reinterpret_cast<unsigned long long*>(c.heap[owner] + rdy_off) + b;
+            st_release_sys(f, p.seq | (unsigned long long)(round + 1));
+          }
+        }
+      } else if (owner == me) {
+        if (threadIdx.x == 0) {
+          const unsigned long long* f = reinterpret_cast<const unsigned long long*>(c.heap[me] + rdy_off) + b;
+          if (!lz_wait_ge(c, f, p.seq | (unsigned long long)(round + 1), 12, p.src)) s_fail = 1;
+        }
+        __syncthreads();
+        if (s_fail) return;
+        const char* mine = c.heap[me] + hoff;
+        if (p.use_mc) push_bytes<true>(c.heap_mc + hoff, mine, len);
+        else relay_push_p2p(c, hoff, mine, len, me);
+      }
+    }
+  }
+  relay_barrier(c, bar_off, p.seq | 2ull, 13);
+  if (p.use_mc && threadIdx.x == 0) fence_proxy_alias();
+}
+
+__global__ void __launch_bounds__(256) wx_relay_kernel(LzDevComm c, WxRelayParams p) { wx_relay_body(c, p); }
+
+// Emulation: grid (G, R), blockIdx.y = rank; the body sees blockIdx.x only.
+__global__ void __launch_bounds__(256) wx_relay_emu_kernel(const LzDevComm* cs, const WxRelayParams* ps) {
+  wx_relay_body(cs[blockIdx.y], ps[blockIdx.y]);
+}
+
+int relay_plan(const LzComm* c, int src, const void* descs, unsigned int ndesc, int use_mc,
+               unsigned long long seq, WxRelayParams* p) {
+  const int W = c->dev.world;
+  if (src < 0 || src >= W) {
+    lz_set_error("relay broadcast: bad src %d", src);
+    return LZE_ARG;
+  }
+  if (use_mc && !c->dev.heap_mc) {
+    lz_set_error("relay broadcast: multicast requested but unavailable");
+    return LZE_UNSUPPORTED;
+  }
+  memset(p, 0, sizeof(*p));
+  p->descs = static_cast<const WxDirectDesc*>(descs);
+  p->ndesc = ndesc;
+  p->src = src;
+  p->use_mc = use_mc;
+  p->seq = seq << 32;
+  return LZE_OK;
+}
+
+}  // namespace
+
+// Every rank calls with the same descriptors' destination offsets (sender's
+// carry the source pointers); use_mc = forward with multimem.st.
+extern "C" int lz_weight_broadcast_relay(LzComm* c, int src, const void* descs, unsigned int ndesc,
+                                         int nblocks, int use_mc, unsigned long long seq, cudaStream_t s) {
+  if (c->dev.world == 1 || ndesc == 0) return LZE_OK;
+  WxRelayParams p;
+  int rc = relay_plan(c, src, descs, ndesc, use_mc, seq, &p);
+  if (rc) return rc;
+  int G = nblocks > 0 ? nblocks : c->sm_count * 2;
+  if (G > LZ_MAX_BLOCKS) G = LZ_MAX_BLOCKS;
+  wx_relay_kernel<<<G, 256, 0, s>>>(c->dev, p);
+  LZ_CUDA_TRY(cudaGetLastError());
+  return LZE_OK;
+}
+
+// Single-GPU emulation of the relay broadcast (peer stores only; descs[r] is
+// rank r's descriptor array). Synchronous.
+extern "C" int lz_emu_weight_broadcast_relay(LzEmu* e, int src, const void* const* descs, unsigned int ndesc,
+                                             int nblocks, unsigned long long seq, cudaStream_t s) {
+  const int R = lz_emu_world(e);
+  WxRelayParams hp[LZ_MAX_RANKS];
+  for (int r = 0; r < R; ++r) {
+    int rc = relay_plan(lz_emu_comm(e, r), src, descs[r], ndesc, 0, seq, &hp[r]);
+    if (rc) return rc;
+  }
+  int G = nblocks > 0 ? nblocks : 8;
+  void* fn = reinterpret_cast<void*>(&wx_relay_emu_kernel);
+  int per_sm = 0;
+  LZ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, 0));
+  if ((long long)G * R > (long long)per_sm * lz_emu_comm(e, 0)->sm_count) {
+    lz_set_error("emulated relay broadcast: %d x %d blocks exceed co-residency", G, R);
+    return LZE_ARG;
+  }
+  static_assert(sizeof(WxRelayParams) * LZ_MAX_RANKS <= 4096, "param buffer");
+  void* dparams = lz_emu_param_buffer(e);
+  LZ_CUDA_TRY(cudaMemcpyAsync(dparams, hp, sizeof(WxRelayParams) * R, cudaMemcpyHostToDevice, s));
+  LzDevComm* dcomms = lz_emu_dev_comms(e);
+  void* args[] = {&dcomms, &dparams};
+  LZ_CUDA_TRY(cudaLaunchCooperativeKernel(fn, dim3(G, R), dim3(256), args, 0, s));
+  LZ_CUDA_TRY(cudaStreamSynchronize(s));
+  return LZE_OK;
+}

@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--include-fill", action="store_true")
     ap.add_argument("--check", action="store_true", help="verify each variant against an fp32 reference")
+    ap.add_argument("--graph", action="store_true",
+                    help="capture the timed iterations of NCCL and the native kernels in one CUDA graph "
+                         "(device time without per-call host overhead); host-staged variants stay eager")
     ap.add_argument("--csv", default=None)
     ap.add_argument("--json", default=None)
     return ap.parse_args()
@@ -56,6 +59,20 @@ def _max(v, ctrl):
     t = torch.tensor([v], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=ctrl)
     return float(t.item())
+
+
+def _capture(fn, fill, iters: int):
+    """One CUDA graph of `iters` back-to-back calls (plus the input refill when timed)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for _ in range(iters):
+            if fill:
+                fill()
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    return g
 
 
 def main():
@@ -122,20 +139,29 @@ def main():
                     fill()
                 fn()
             torch.cuda.synchronize()
+            graph = None
+            if a.graph and v not in HOST:
+                graph = _capture(fn, fill, a.iters)
+                graph.replay()  # warm the graph once (same collective count on every rank)
+                torch.cuda.synchronize()
             dist.barrier(group=ctrl)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             t0 = time.perf_counter()
-            for _ in range(a.iters):
-                if fill:
-                    fill()
-                fn()
+            if graph is not None:
+                graph.replay()
+            else:
+                for _ in range(a.iters):
+                    if fill:
+                        fill()
+                    fn()
             e1.record()
             torch.cuda.synchronize()
             t1 = time.perf_counter()
             cuda_ms = _max(e0.elapsed_time(e1) / a.iters, ctrl)
             wall_ms = _max((t1 - t0) * 1e3 / a.iters, ctrl)
             comm.check()
+            del graph  # graphs holding NCCL work are released before the group is destroyed
             ok = None
             if a.check and v in NATIVE | {"compressed"}:
                 xs.copy_(src)
@@ -183,7 +209,9 @@ def main():
         csvfmt.write_sidecar(a.csv, {"bench": "allreduce_sweep", "world": world, "dtype": a.dtype,
                                      "iters": a.iters, "warmup": a.warmup, "include_fill": a.include_fill,
                                      "multicast": comm.has_multicast,
-                                     "timing": "CUDA events per rank, max over ranks"})
+                                     "graph": a.graph,
+                                     "timing": "CUDA events per rank, max over ranks" +
+                                               ("; timed iterations replayed from one CUDA graph" if a.graph else "")})
     if rank == 0 and a.json:
         with open(a.json, "w") as f:
             json.dump(rows, f)

@@ -112,6 +112,32 @@ class EmulatedWorld:
                                               int(broadcast_all), sq, torch.cuda.current_stream().cuda_stream)
         _native.check(rc, "emulated weight transfer")
 
+    def broadcast_relay(self, src: int, dst_tensors, src_tensors, nblocks: int = 8):
+        """Relay broadcast (peer stores) from emulated rank `src` into every
+        rank's symmetric tensors dst_tensors[r] (lists from ``empty``)."""
+        from . import weights  # noqa: F401  (declares the native signature)
+
+        R = self.world
+        if not hasattr(self, "_relay_seq"):
+            self._relay_seq = {}
+        seq = self._relay_seq.get(src, 0) + 1
+        self._relay_seq[src] = seq
+        keep, ptrs = [], []
+        for r in range(R):
+            base = self._lib.lz_emu_heap_ptr(self._emu, r)
+            rows = []
+            for i, d in enumerate(dst_tensors[r]):
+                nbytes = d.numel() * d.element_size()
+                srcp = src_tensors[i].data_ptr() if r == src else 0
+                rows.append([srcp, d.data_ptr() - base, nbytes, 0])
+            t = torch.tensor(rows, dtype=torch.int64, device=f"cuda:{self.device}")
+            keep.append(t)
+            ptrs.append(t.data_ptr())
+        arr = (C.c_void_p * R)(*ptrs)
+        rc = self._lib.lz_emu_weight_broadcast_relay(self._emu, src, arr, len(dst_tensors[0]), nblocks, seq,
+                                                     torch.cuda.current_stream().cuda_stream)
+        _native.check(rc, "emulated relay broadcast")
+
     def status(self, r: int) -> int:
         return self._lib.lz_emu_status(self._emu, r)
 

@@ -42,6 +42,10 @@ _native_sigs.add_cuda({
                            C.c_int, C.c_int, C.POINTER(C.c_uint64), C.c_void_p),
     "lz_weight_transfer_direct": (C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_uint, C.c_void_p, C.c_uint,
                                   C.c_int, C.c_int, C.POINTER(C.c_uint64), C.c_void_p),
+    "lz_weight_broadcast_relay": (C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_uint, C.c_int, C.c_int,
+                                  C.c_uint64, C.c_void_p),
+    "lz_emu_weight_broadcast_relay": (C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_void_p), C.c_uint, C.c_int,
+                                      C.c_uint64, C.c_void_p),
 })
 
 TG = 32768
@@ -180,13 +184,20 @@ class WeightTransfer:
         t = torch.tensor(rows, dtype=torch.int64).pin_memory()
         return t.to(f"cuda:{comm.device}", non_blocking=True), len(rows)
 
-    def broadcast_direct(self, dst_tensors, src: int, src_tensors=None, nblocks: int = 0) -> None:
+    def broadcast_direct(self, dst_tensors, src: int, src_tensors=None, nblocks: int = 0,
+                         relay: bool | None = None) -> None:
         """Zero-copy raw broadcast into symmetric destination tensors.
 
         Every rank passes its symmetric destination tensors (allocated with
         ``comm.empty`` in the same order on all ranks); the sender also passes
-        ``src_tensors`` (default: its own destination tensors). One multimem
-        store per 16 bytes lands in every receiver's tensor.
+        ``src_tensors`` (default: its own destination tensors).
+
+        With more than two ranks (``relay`` default) the bytes are relayed:
+        the sender hands each 256 KB chunk to one owner rank, which forwards
+        it to every other rank (multimem.st through the switch when multicast
+        is available), so all GPUs' NVLink egress carries the broadcast and
+        every receiver takes in each byte once. Otherwise the sender stores
+        every chunk into every receiver itself.
         """
         comm = self.comm
         if comm.world == 1:
@@ -198,6 +209,18 @@ class WeightTransfer:
         mask = ((1 << comm.world) - 1) & ~(1 << src)
         s = self.bcast_seq.get(src, 0) + 1
         self.bcast_seq[src] = s
+        if relay is None:
+            relay = comm.world > 2
+        if relay:
+            descs, nd = self._direct_descs(dst_tensors, (src_tensors if src_tensors is not None else dst_tensors)
+                                           if me == src else None)
+            st = torch.cuda.current_stream(comm.device)
+            rc = comm._lib.lz_weight_broadcast_relay(comm.handle, src, descs.data_ptr(), nd,
+                                                     nblocks or min(comm.sm_count * 2, 512),
+                                                     int(comm.has_multicast), s, st.cuda_stream)
+            _native.check(rc, "relay weight broadcast")
+            self._keep = descs
+            return
         if me == src:
             descs, nd = self._direct_descs(dst_tensors, src_tensors if src_tensors is not None else dst_tensors)
             role = 0

@@ -44,3 +44,33 @@ def test_emulated_transfer_repeated(world3, encode, bcast):
             assert world3.status(r) == 0
             for a, b in zip(recv[r], src_t):
                 assert torch.equal(a.view(torch.uint8), b.view(torch.uint8)), (it, r, a.shape)
+
+
+@pytest.mark.parametrize("src", [0, 2])
+def test_emulated_relay_broadcast(src):
+    """Relay broadcast: chunks dealt to owner ranks that forward them; every
+    rank's symmetric tensors must end bit-identical to the sender's source,
+    over repeated calls with changing data and a sender whose source is not
+    its own destination."""
+    from results_b200.parallel.emulate import EmulatedWorld
+
+    R = 4
+    w = EmulatedWorld(R, heap_bytes=(256 << 20))
+    try:
+        shapes = [(1000, 512), (7,), (3, 32768), (77, 129), (700001,), (1 << 20,)]
+        dst = [w.empty(s, torch.bfloat16) for s in shapes]  # dst[i][r]
+        per_rank = [[dst[i][r] for i in range(len(shapes))] for r in range(R)]
+        for it in range(3):
+            g = torch.Generator(device="cuda").manual_seed(1000 * it + src)
+            srcs = [(torch.randn(s, device="cuda", generator=g) * 0.02).to(torch.bfloat16) for s in shapes]
+            for r in range(R):
+                for t in per_rank[r]:
+                    t.fill_(float(r + 1))
+            w.broadcast_relay(src, per_rank, srcs, nblocks=6)
+            torch.cuda.synchronize()
+            for r in range(R):
+                assert w.status(r) == 0
+                for a, b in zip(per_rank[r], srcs):
+                    assert torch.equal(a.view(torch.uint8), b.view(torch.uint8)), (it, r, a.shape)
+    finally:
+        w.close()
