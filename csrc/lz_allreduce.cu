@@ -406,7 +406,7 @@ __device__ __forceinline__ void ring_body(const LzDevComm& c, const ArParams& P)
         }
         if (k < hops) st_v4(right_slots + sslot * tile_vecs + i, data);
       }
-      publish_block_writes();
+      publish_block_writes(c);
       if (threadIdx.x == 0) {
         fence_sys();
         if (k > 0) st_release_sys(left_credit, base + q_recv + 1);
@@ -585,6 +585,10 @@ static int init_comm_state(LzComm* c, int dev, size_t oneshot_bytes, size_t stag
   c->status_host = st_host;
   c->dev.status = st_dev;
   c->dev.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  {
+    const char* fa = getenv("LZ_FENCE_ALL");
+    c->dev.fence_all = (fa && atoi(fa) != 0) ? 1 : 0;
+  }
   c->dev.flags_off = 0;
   c->dev.flags = reinterpret_cast<unsigned long long*>(c->dev.heap[c->dev.rank]);
   LZ_CUDA_TRY(cudaMemset(c->dev.heap[c->dev.rank], 0, kLzFlagsBytes));

@@ -255,12 +255,15 @@ LZ_DEV unsigned long long* peer_flags(const LzDevComm& c, int peer) {
   return reinterpret_cast<unsigned long long*>(c.heap[peer] + c.flags_off);
 }
 
-// Every thread fences its own peer/multicast writes at system scope before
-// the CTA barrier: a fence covers the issuing warp's outstanding stores, so a
-// single signalling thread's fence is not enough to publish the stores of the
-// other warps that are still in flight on NVLink.
-LZ_DEV void publish_block_writes() {
-  fence_sys();
+// CTA barrier ahead of a release signal. The signalling thread then issues
+// fence.acq_rel.sys + st.release.sys; by the PTX memory model the barrier
+// puts every thread's earlier stores in causality order before that release,
+// so they are published with it. `fence_all` (environment LZ_FENCE_ALL=1)
+// additionally makes every thread fence its own stores first: a diagnostic
+// switch for ordering questions, off by default (it costs a system-scope
+// fence per warp per signal).
+LZ_DEV void publish_block_writes(const LzDevComm& c) {
+  if (c.fence_all) fence_sys();
   __syncthreads();
 }
 
@@ -271,7 +274,7 @@ LZ_DEV void publish_block_writes() {
 LZ_DEV bool block_barrier(const LzDevComm& c, unsigned long long epoch, int phase) {
   __shared__ int s_fail;
   if (threadIdx.x == 0) s_fail = 0;
-  publish_block_writes();
+  publish_block_writes(c);
   const int t = threadIdx.x;
   if (t < c.world && t != c.rank) {
     const unsigned long long v = flag_value(epoch, phase);
@@ -287,7 +290,7 @@ LZ_DEV bool block_barrier(const LzDevComm& c, unsigned long long epoch, int phas
 LZ_DEV bool pair_barrier(const LzDevComm& c, unsigned long long epoch, int phase, int partner) {
   __shared__ int s_fail2;
   if (threadIdx.x == 0) s_fail2 = 0;
-  publish_block_writes();
+  publish_block_writes(c);
   if (threadIdx.x == 0) {
     const unsigned long long v = flag_value(epoch, phase);
     fence_sys();
@@ -303,7 +306,7 @@ LZ_DEV bool pair_barrier(const LzDevComm& c, unsigned long long epoch, int phase
 LZ_DEV bool block_barrier_mc(const LzDevComm& c, unsigned long long epoch, int phase) {
   __shared__ int s_fail3;
   if (threadIdx.x == 0) s_fail3 = 0;
-  publish_block_writes();
+  publish_block_writes(c);
   const unsigned long long v = flag_value(epoch, phase);
   if (threadIdx.x == 0) {
     fence_sys();

@@ -30,5 +30,6 @@ struct LzDevComm {
   int* abort_flag;                // local: set when any block gave up waiting
   int* status;                    // host-mapped: first error (code | where)
   unsigned long long timeout_ns;  // bound of every flag wait
+  int fence_all;                  // 1: every thread fences its peer stores before a signal
 };
 

@@ -193,7 +193,7 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
           }
         }
       }
-      publish_block_writes();
+      publish_block_writes(c);
       if (p.use_mc) {
         if (threadIdx.x == 0) {
           fence_sys();
@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(256) wx_direct_kernel(LzDevComm c, WxDirectPar
         }
       }
     }
-    publish_block_writes();
+    publish_block_writes(c);
     const int t = threadIdx.x;
     if (t < W && ((p.recv_mask >> t) & 1u)) {
       fence_sys();
@@ -537,7 +537,7 @@ struct WxRelayParams {
 LZ_DEV bool relay_barrier(const LzDevComm& c, size_t bar_off, unsigned long long v, int phase) {
   __shared__ int s_fail_rb;
   if (threadIdx.x == 0) s_fail_rb = 0;
-  publish_block_writes();
+  publish_block_writes(c);
   const int t = threadIdx.x;
   if (t < c.world && t != c.rank) {
     unsigned long long* mine = reinterpret_cast<unsigned long long*>(c.heap[t] + bar_off) +
@@ -589,7 +589,7 @@ __device__ __forceinline__ void wx_relay_body(const LzDevComm& c, const WxRelayP
           else relay_push_p2p(c, hoff, d.src + off, len, -1);
         } else {
           push_bytes<false>(c.heap[owner] + hoff, d.src + off, len);
-          publish_block_writes();
+          publish_block_writes(c);
           if (threadIdx.x == 0) {
             fence_sys();
             unsigned long long* f = reinterpret_cast<unsigned long long*>(c.heap[owner] + rdy_off) + b;

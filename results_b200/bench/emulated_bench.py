@@ -52,7 +52,7 @@ def main(argv=None):
     heap = 2 * n * es + 2 * oneshot + stage + (16 << 20)
     w = EmulatedWorld(R, heap_bytes=heap, oneshot_bytes=oneshot, stage_bytes=stage)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    ar_blocks = args.nblocks or max(1, 2 * sms // R)  # R grids of 512 threads stay co-resident
+    ar_blocks = args.nblocks or max(1, sms // R)  # R grids of 512-thread CTAs stay co-resident
     ins = w.empty((n,), dt)
     outs = w.empty((n,), dt)
     g = torch.Generator(device="cuda").manual_seed(7)
