@@ -491,7 +491,97 @@ __device__ __forceinline__ void barrier_body(const LzDevComm& c, const ArParams&
   epoch_advance(c);
 }
 
-enum ArKind { K_ONESHOT, K_TWOSHOT, K_TWOSHOT_SYM, K_NVLS, K_NVLS_ONESHOT, K_RING, K_RHD, K_BARRIER };
+// ----------------------------------------------------------------------------
+// low-latency one-shot for small messages: every rank pushes its input
+// straight into each peer's receive area as 8-byte words {4 payload bytes,
+// 32-bit call flag}. A naturally aligned 64-bit store is single-copy atomic,
+// so a word whose flag equals this call's value carries this call's payload:
+// no barrier and no fence, one NVLink traversal. Receivers poll their own
+// memory and reduce in rank order (fp32), bit-identical to the other
+// algorithms. Areas are double-buffered by call parity: a rank reaches call
+// e+2 (reusing parity e&1) only after every peer has started call e+1, i.e.
+// finished reading call e. Flags are an odd-multiplier hash of the call
+// number with the low bit set: never 0 (zeroed memory) and distinct across
+// 2^31 uses of one parity.
+// Params: a = heap offset of the areas, b = bytes per parity, c = bytes per
+// source rank (2 x the largest message).
+// ----------------------------------------------------------------------------
+LZ_DEV uint32_t ll_flag(unsigned long long epoch) {
+  return ((uint32_t)(epoch + 1ull) * 0x9E3779B1u) | 1u;
+}
+LZ_DEV void st_ll2(void* p, unsigned long long a, unsigned long long b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+LZ_DEV void ld_ll2(const void* p, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Polls the 4 words of one 16-byte payload vector until all carry `flag`.
+LZ_DEV uint4 ll_recv(const LzDevComm& c, const char* p, uint32_t flag, bool& ok, int peer) {
+  unsigned long long w0, w1, w2, w3;
+  ld_ll2(p, w0, w1);
+  ld_ll2(p + 16, w2, w3);
+  const unsigned long long t0 = globaltimer();
+  unsigned int it = 0;
+  while (ok && ((uint32_t)(w0 >> 32) != flag || (uint32_t)(w1 >> 32) != flag ||
+                (uint32_t)(w2 >> 32) != flag || (uint32_t)(w3 >> 32) != flag)) {
+    if ((++it & 1023u) == 0u) {
+      if (ld_volatile_i32(c.abort_flag)) {
+        ok = false;
+        break;
+      }
+      if (globaltimer() - t0 > c.timeout_ns) {
+        lz_report(c, LZ_ERR_TIMEOUT, 9, peer);
+        ok = false;
+        break;
+      }
+    }
+    ld_ll2(p, w0, w1);
+    ld_ll2(p + 16, w2, w3);
+  }
+  return make_uint4((uint32_t)w0, (uint32_t)w1, (uint32_t)w2, (uint32_t)w3);
+}
+
+template <int DT>
+__device__ __forceinline__ void ll_oneshot_body(const LzDevComm& c, const ArParams& P) {
+  using V = Vec<DT>;
+  const unsigned long long epoch = epoch_read(c);
+  const uint32_t flag = ll_flag(epoch);
+  const unsigned long long fhi = (unsigned long long)flag << 32;
+  const size_t area = P.a + (epoch & 1ull) * P.b, slot = P.c;
+  const int W = c.world, me = c.rank;
+  const size_t nv = P.bytes / 16;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint4* in = reinterpret_cast<const uint4*>(P.in);
+  for (size_t i = i0; i < nv; i += stride) {
+    const uint4 v = in[i];
+    const unsigned long long w0 = fhi | v.x, w1 = fhi | v.y, w2 = fhi | v.z, w3 = fhi | v.w;
+#pragma unroll
+    for (int r = 0; r < LZ_MAX_RANKS; ++r) {
+      if (r >= W || r == me) continue;
+      char* dst = c.heap[r] + area + (size_t)me * slot + i * 32;
+      st_ll2(dst, w0, w1);
+      st_ll2(dst + 16, w2, w3);
+    }
+  }
+  bool ok = true;
+  for (size_t i = i0; i < nv; i += stride) {
+    const uint4 mine = in[i];
+    float acc[V::N];
+#pragma unroll
+    for (int r = 0; r < LZ_MAX_RANKS; ++r) {
+      if (r >= W) continue;
+      const uint4 v = r == me ? mine : ll_recv(c, c.heap[me] + area + (size_t)r * slot + i * 32, flag, ok, r);
+      if (r == 0) V::load(acc, v);
+      else V::add(acc, v);
+    }
+    st_v4(reinterpret_cast<uint4*>(P.out) + i, V::pack(acc));
+  }
+  epoch_advance(c);
+}
+
+enum ArKind { K_ONESHOT, K_TWOSHOT, K_TWOSHOT_SYM, K_NVLS, K_NVLS_ONESHOT, K_RING, K_RHD, K_BARRIER, K_LL };
 
 template <int DT, int K>
 __device__ __forceinline__ void ar_body(const LzDevComm& c, const ArParams& p) {
@@ -502,6 +592,7 @@ __device__ __forceinline__ void ar_body(const LzDevComm& c, const ArParams& p) {
   else if constexpr (K == K_NVLS_ONESHOT) nvls_oneshot_body<DT>(c, p);
   else if constexpr (K == K_RING) ring_body<DT>(c, p);
   else if constexpr (K == K_RHD) rhd_body<DT>(c, p);
+  else if constexpr (K == K_LL) ll_oneshot_body<DT>(c, p);
   else barrier_body(c, p);
 }
 
@@ -562,7 +653,9 @@ static int init_comm_state(LzComm* c, int dev, size_t oneshot_bytes, size_t stag
                            double timeout_s) {
   c->oneshot_bytes = (oneshot_bytes + 4095) / 4096 * 4096;
   c->oneshot_off = kLzFlagsBytes;
-  c->stage_off = c->oneshot_off + 2 * c->oneshot_bytes;
+  c->ll_off = c->oneshot_off + 2 * c->oneshot_bytes;
+  c->ll_bytes = (size_t)c->dev.world * 2 * kLzLlMaxBytes;  // per parity
+  c->stage_off = c->ll_off + 2 * c->ll_bytes;
   c->stage_bytes = (stage_bytes + 4095) / 4096 * 4096;
   c->user_off = c->stage_off + c->stage_bytes;
   c->user_off = (c->user_off + (2u << 20) - 1) / (2u << 20) * (2u << 20);
@@ -592,6 +685,8 @@ static int init_comm_state(LzComm* c, int dev, size_t oneshot_bytes, size_t stag
   c->dev.flags_off = 0;
   c->dev.flags = reinterpret_cast<unsigned long long*>(c->dev.heap[c->dev.rank]);
   LZ_CUDA_TRY(cudaMemset(c->dev.heap[c->dev.rank], 0, kLzFlagsBytes));
+  LZ_CUDA_TRY(cudaMemset(c->dev.heap[c->dev.rank] + c->ll_off, 0, 2 * c->ll_bytes));
+  LZ_CUDA_TRY(cudaDeviceSynchronize());  // zeroed before any peer can push (callers barrier next)
   int sms = 0;
   LZ_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   c->sm_count = sms;
@@ -740,6 +835,24 @@ static int plan_allreduce(const LzComm* c, const void* in, void* out, size_t cou
       }
       break;
     }
+    case LZ_ALGO_LL: {
+      if (bytes > kLzLlMaxBytes || !aligned) {
+        lz_set_error("low-latency one-shot needs 16-byte aligned pointers and sizes up to %zu bytes (got %zu)",
+                     (size_t)kLzLlMaxBytes, bytes);
+        return LZE_ARG;
+      }
+      if (auto_shape) nthreads = nv >= 512 * 8 ? 512 : (nv >= 128 ? 256 : 128);
+      P.nthreads = nthreads;
+      // every block waits only on the same-index blocks of its peers; G never
+      // exceeds one block per SM so all of them are resident
+      P.G = nblocks > 0 ? clamp_int(nblocks, 1, smax)
+                        : clamp_int((long long)((nv + nthreads - 1) / nthreads), 1, smax);
+      P.p.a = c->ll_off;
+      P.p.b = c->ll_bytes;
+      P.p.c = 2 * kLzLlMaxBytes;
+      P.kind = K_LL;
+      break;
+    }
     case LZ_ALGO_TWOSHOT: {
       const size_t in_off = lz_comm_heap_offset(c, in, bytes);
       const size_t out_off = lz_comm_heap_offset(c, out, bytes);
@@ -850,6 +963,7 @@ static void* kernel_ptr(int kind, bool emu) {
     LZ_K(K_RING)
     LZ_K(K_RHD)
     LZ_K(K_BARRIER)
+    LZ_K(K_LL)
 #undef LZ_K
   }
   return nullptr;

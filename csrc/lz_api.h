@@ -71,6 +71,7 @@ int lz_comm_epoch(LzComm* c, unsigned long long* epoch, cudaStream_t s);
 #define LZ_ALGO_RING 3
 #define LZ_ALGO_RHD 4
 #define LZ_ALGO_NVLS_ONESHOT 5
+#define LZ_ALGO_LL 6  /* low-latency one-shot (flag-in-data words), <= 256 KB */
 
 // Sum-allreduce of `count` elements. `in`/`out` may alias; when they lie in
 // the heap's user region the zero-copy symmetric path is used.

@@ -24,6 +24,7 @@ int lz_heap_world(LzHeap* h);
 
 // Communicator: device-visible state plus the heap layout.
 static constexpr size_t kLzFlagsBytes = 1 << 20;
+static constexpr size_t kLzLlMaxBytes = 256u << 10;  // largest low-latency one-shot message
 
 struct LzComm {
   LzHeap* heap;           // nullptr for emulated ranks
@@ -32,6 +33,8 @@ struct LzComm {
   LzDevComm dev;          // copied by value into every launch
   size_t oneshot_off;     // two stages of oneshot_bytes each (double buffered)
   size_t oneshot_bytes;
+  size_t ll_off;          // low-latency one-shot receive areas (two parities)
+  size_t ll_bytes;        // bytes per parity: world x 2 x kLzLlMaxBytes
   size_t stage_off;       // general staging region
   size_t stage_bytes;
   size_t user_off;        // start of the user-allocatable region

@@ -31,9 +31,9 @@ LABELS = {
     "rhd_sendrecv": "RHD", "twoshot_collective": "2Shot", "twoshot": "P2P", "ring": "RingP2P",
     "compressed_ring": "Comp", "compressed_twoshot": "NoSize", "oneshot": "OneShot", "nvls": "NVLS",
     "nvls_oneshot": "NVLSOneShot", "rhd": "RHDP2P", "compressed": "CompNative",
-    "multichannel_ring": "MCRing", "copy_engine": "P2PnoPA",
+    "multichannel_ring": "MCRing", "copy_engine": "P2PnoPA", "ll": "LL", "auto": "Auto",
 }
-NATIVE = {"oneshot", "twoshot", "nvls", "nvls_oneshot", "ring", "rhd"}
+NATIVE = {"oneshot", "twoshot", "nvls", "nvls_oneshot", "ring", "rhd", "ll", "auto"}
 HOST = {"naive", "naive_twoshot", "ring_sendrecv", "rhd_sendrecv", "twoshot_collective", "multichannel_ring"}
 
 
@@ -87,7 +87,7 @@ def main():
     import results_b200 as lz
     from results_b200.config import Config, MiB
     from results_b200.parallel import compressed as cz
-    from results_b200.parallel import sendrecv
+    from results_b200.parallel import sendrecv, tuning
 
     dtype = getattr(torch, a.dtype)
     es = torch.empty((), dtype=dtype).element_size()
@@ -115,12 +115,17 @@ def main():
                 continue
             if v in ("oneshot", "nvls_oneshot") and nbytes > 8 * MiB:
                 continue
+            if v == "ll" and (nbytes > 256 * 1024 or nbytes % 16):
+                continue
             if v in ("rhd", "rhd_sendrecv") and world & (world - 1):
                 continue
             xs.copy_(src)
             if v == "nccl":
                 buf = src.clone()
                 fn = lambda: dist.all_reduce(buf)
+            elif v == "auto":
+                algo = tuning.choose(nbytes, world, comm.has_multicast, symmetric=True)
+                fn = lambda algo=algo: comm.allreduce_(xs, ys, algo=algo)
             elif v in NATIVE:
                 fn = lambda v=v: comm.allreduce_(xs, ys, algo=v)
             elif v == "compressed":
@@ -172,7 +177,7 @@ def main():
                 for r in range(world):
                     gg = torch.Generator(device="cuda").manual_seed(100 + r)
                     acc += (torch.randn(n, device="cuda", generator=gg)[:m] * 1e-2).to(dtype).float()
-                ok = bool(torch.equal(ys[:m], acc.to(dtype))) if v in ("oneshot", "twoshot", "compressed") \
+                ok = bool(torch.equal(ys[:m], acc.to(dtype))) if v in ("oneshot", "twoshot", "compressed", "ll") \
                     else float(((ys[:m].float() - acc).abs().max() / acc.abs().max()).item())
             ratio = None
             if v == "compressed" and rank == 0:

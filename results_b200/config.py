@@ -92,4 +92,6 @@ class Config:
     def total_heap_bytes(self) -> int:
         if self.heap_bytes:
             return self.heap_bytes
-        return (1 * MiB) + 2 * self.oneshot_bytes + self.stage_bytes + self.user_bytes + 4 * MiB
+        # flags (1 MiB) + one-shot double buffer + low-latency areas (2 parities x
+        # up to 8 ranks x 2 x 256 KB = 8 MiB) + stage + user + alignment slack
+        return (1 * MiB) + 2 * self.oneshot_bytes + 8 * MiB + self.stage_bytes + self.user_bytes + 4 * MiB

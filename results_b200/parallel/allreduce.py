@@ -6,7 +6,8 @@ benchmark driver (single_node_nccl_allreduce_benchmark/benchmark_both.py:372-383
 
 * native sm_100a kernels over NVLink peer memory / NVLS (CUDA tensors):
   ``oneshot``, ``twoshot`` (alias ``p2p``), ``nvls``, ``nvls_oneshot``,
-  ``ring`` (alias ``ringp2p``), ``rhd``;
+  ``ring`` (alias ``ringp2p``), ``rhd``, ``ll`` (low-latency one-shot,
+  flag-in-data pushes, messages up to 256 KB);
 * NCCL baseline: ``nccl`` (``dist.all_reduce``);
 * host-orchestrated send/recv reference algorithms (any backend, also CPU):
   ``naive``, ``naive_twoshot``, ``ring_sendrecv``, ``rhd_sendrecv``,
@@ -23,7 +24,7 @@ from .comm import Communicator
 
 _DEFAULT: Communicator | None = None
 
-NATIVE = {"oneshot", "twoshot", "nvls", "nvls_oneshot", "ring", "rhd"}
+NATIVE = {"oneshot", "twoshot", "nvls", "nvls_oneshot", "ring", "rhd", "ll"}
 ALIASES = {"p2p": "twoshot", "ringp2p": "ring", "two_shot": "twoshot", "one_shot": "oneshot"}
 HOST_ALGOS = {"naive", "naive_twoshot", "ring_sendrecv", "rhd_sendrecv", "twoshot_collective",
               "multichannel_ring", "hierarchical", "pipelined_twoshot"}
@@ -74,6 +75,13 @@ def allreduce(t: torch.Tensor, algo: str = "auto", out: torch.Tensor | None = No
         algo = select_algo(t.numel() * t.element_size(), comm.world, comm.has_multicast,
                            comm.is_symmetric(t) and (out is None or comm.is_symmetric(out)),
                            comm.config)
+        if algo != "oneshot" and (t.data_ptr() % 16 or (out is not None and out.data_ptr() % 16)):
+            if t.numel() * t.element_size() <= comm.config.oneshot_bytes:
+                algo = "oneshot"
+            else:  # vector kernels need 16-byte aligned buffers: go through an aligned copy
+                tmp = t.contiguous().clone()
+                comm.allreduce_(tmp, algo="twoshot" if tmp.numel() * tmp.element_size() % 16 == 0 else "oneshot")
+                return (t if out is None else out).copy_(tmp)
     if algo not in NATIVE:
         raise ValueError(f"unknown allreduce algorithm {algo!r}")
     return comm.allreduce_(t, out, algo=algo)

@@ -30,6 +30,7 @@ ALGOS = {
     "ring": 3,
     "rhd": 4,
     "nvls_oneshot": 5,
+    "ll": 6,
 }
 
 

@@ -49,6 +49,28 @@ def test_oneshot_bitexact(emu_worlds, R, dtype, n):
 
 @pytest.mark.parametrize("R", [2, 4, 8])
 @pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("n", [8, 1000, 4096, 1 << 16])
+def test_ll_bitexact(emu_worlds, R, dtype, n):
+    """Low-latency one-shot: flag-in-data words, parity areas reused across
+    calls (interleaved with one-shot so the call parity moves on)."""
+    w = emu_worlds[R]
+    es = torch.empty((), dtype=dtype).element_size()
+    if (n * es) % 16:
+        pytest.skip("ll needs a multiple of 16 bytes")
+    ref = None
+    for it in range(5):
+        xs = _inputs(R, n, dtype, seed=n + R + it)
+        outs = [torch.empty_like(x) for x in xs]
+        w.allreduce(xs, outs, "ll" if it != 2 else "oneshot", nblocks=8, nthreads=256)
+        torch.cuda.synchronize()
+        ref = _ref(xs)
+        for r in range(R):
+            assert w.status(r) == 0
+            assert torch.equal(outs[r], ref), f"call {it} rank {r} differs"
+
+
+@pytest.mark.parametrize("R", [2, 4, 8])
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("n", [1024, 1 << 16, (1 << 20) + 64])
 def test_twoshot_bitexact(emu_worlds, R, dtype, n):
     w = emu_worlds[R]

@@ -78,6 +78,9 @@ CASES = [
     ("nvls", "float32", 1 << 20, False, False),
     ("nvls", "bfloat16", (1 << 20) + 64, False, False),
     ("nvls_oneshot", "bfloat16", 1 << 14, False, False),
+    ("ll", "bfloat16", 1000, False, True),
+    ("ll", "float32", 1 << 16, False, True),
+    ("ll", "bfloat16", 1 << 17, False, True),
     ("compressed", "bfloat16", (1 << 20) + 48, False, True),
     ("compressed_mc", "bfloat16", 1 << 21, False, True),
     ("compressed", "float32", 300_000, False, True),
