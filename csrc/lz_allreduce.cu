@@ -408,7 +408,6 @@ __device__ __forceinline__ void ring_body(const LzDevComm& c, const ArParams& P)
       }
       publish_block_writes(c);
       if (threadIdx.x == 0) {
-        fence_sys();
         if (k > 0) st_release_sys(left_credit, base + q_recv + 1);
         if (k < hops) st_release_sys(right_ready, base + q_send + 1);
       }
@@ -681,6 +680,8 @@ static int init_comm_state(LzComm* c, int dev, size_t oneshot_bytes, size_t stag
   {
     const char* fa = getenv("LZ_FENCE_ALL");
     c->dev.fence_all = (fa && atoi(fa) != 0) ? 1 : 0;
+    const char* pr = getenv("LZ_POLL");
+    c->dev.poll_relaxed = (pr && atoi(pr) == 1) ? 1 : 0;
   }
   c->dev.flags_off = 0;
   c->dev.flags = reinterpret_cast<unsigned long long*>(c->dev.heap[c->dev.rank]);

@@ -202,7 +202,6 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
           multimem_st_release_u64(f, p.seq[0] | (unsigned long long)(i + 1));
         }
       } else if (t_r < W && ((p.recv_mask >> t_r) & 1u)) {
-        fence_sys();
         unsigned long long* f = reinterpret_cast<unsigned long long*>(c.heap[t_r] + p.ready_off) +
                                 (size_t)p.src * LZ_MAX_BLOCKS + b;
         st_release_sys(f, p.seq[t_r] | (unsigned long long)(i + 1));
@@ -217,7 +216,6 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
     const uint32_t g = (uint32_t)p.group;
     const uint32_t nitems = (p.ntg + g - 1) / g;
     if (threadIdx.x == 0 && b < nitems) {
-      fence_sys();
       st_release_sys(credit, p.seq[0]);  // started: the sender may fill the slots
     }
     for (uint32_t i = 0; b + (uint64_t)i * G < nitems; ++i) {
@@ -254,7 +252,6 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
       }
       __syncthreads();
       if (threadIdx.x == 0) {
-        fence_sys();
         st_release_sys(credit, p.seq[0] | (unsigned long long)(i + 1));
       }
     }
@@ -450,7 +447,6 @@ __global__ void __launch_bounds__(256) wx_direct_kernel(LzDevComm c, WxDirectPar
     publish_block_writes(c);
     const int t = threadIdx.x;
     if (t < W && ((p.recv_mask >> t) & 1u)) {
-      fence_sys();
       unsigned long long* f = reinterpret_cast<unsigned long long*>(c.heap[t] + p.ready_off) +
                               (size_t)p.src * LZ_MAX_BLOCKS + b;
       st_release_sys(f, p.seq[t] | 1ull);
@@ -459,7 +455,6 @@ __global__ void __launch_bounds__(256) wx_direct_kernel(LzDevComm c, WxDirectPar
     if (threadIdx.x == 0) {
       unsigned long long* cr = reinterpret_cast<unsigned long long*>(c.heap[p.src] + p.credit_off) +
                                (size_t)b * LZ_MAX_RANKS + c.rank;
-      fence_sys();
       st_release_sys(cr, p.seq[0] | 1ull);  // clear to send
       const unsigned long long* f = reinterpret_cast<const unsigned long long*>(c.heap[c.rank] + p.ready_off) +
                                     (size_t)p.src * LZ_MAX_BLOCKS + b;
@@ -542,7 +537,6 @@ LZ_DEV bool relay_barrier(const LzDevComm& c, size_t bar_off, unsigned long long
   if (t < c.world && t != c.rank) {
     unsigned long long* mine = reinterpret_cast<unsigned long long*>(c.heap[t] + bar_off) +
                                (size_t)blockIdx.x * LZ_MAX_RANKS + c.rank;
-    fence_sys();
     st_release_sys(mine, v);
     const unsigned long long* theirs = reinterpret_cast<const unsigned long long*>(c.heap[c.rank] + bar_off) +
                                        (size_t)blockIdx.x * LZ_MAX_RANKS + t;
@@ -591,7 +585,6 @@ __device__ __forceinline__ void wx_relay_body(const LzDevComm& c, const WxRelayP
           push_bytes<false>(c.heap[owner] + hoff, d.src + off, len);
           publish_block_writes(c);
           if (threadIdx.x == 0) {
-            fence_sys();
             unsigned long long* f = reinterpret_cast<unsigned long long*>(c.heap[owner] + rdy_off) + b;
             st_release_sys(f, p.seq | (unsigned long long)(round + 1));
           }

@@ -7,6 +7,7 @@ re-designed for 8xB200 with NVLink 5 / NVSwitch):
 * ``allreduce(t, algo="auto")`` -- one-shot, two-shot, NVLS, ring, RHD native
   kernels; NCCL baseline; send/recv reference algorithms
 * ``compressed_allreduce(t)`` -- lossless split+rANS compressed two-shot
+* ``all_to_all(x, compress=False)`` -- raw or split+rANS compressed all-to-all
 * ``send_weights`` / ``recv_weights`` / ``broadcast_weights`` -- RL weight
   update transfer (raw / split+rANS), chunk-pipelined
 * ``encode`` / ``decode`` -- the LZC1 lossless float codec
@@ -33,6 +34,10 @@ def __getattr__(name):
         from .parallel import compressed
 
         return getattr(compressed, name)
+    if name in ("all_to_all",):
+        from .parallel import alltoall
+
+        return getattr(alltoall, name)
     if name in ("send_weights", "recv_weights", "broadcast_weights", "WeightTransfer"):
         from .parallel import weights
 

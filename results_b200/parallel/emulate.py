@@ -112,6 +112,20 @@ class EmulatedWorld:
                                               int(broadcast_all), sq, torch.cuda.current_stream().cuda_stream)
         _native.check(rc, "emulated weight transfer")
 
+    def all_to_all(self, ins, outs, compress: bool = False, nblocks: int = 0):
+        """ins[r] / outs[r]: rank r's W equal chunks (outs symmetric or not)."""
+        from . import alltoall  # noqa: F401  (declares the native signature)
+
+        R = self.world
+        x = ins[0]
+        dt = lz_dtype(x.dtype) if x.dtype in alltoall.COMPRESSIBLE else 3
+        chunk = x.numel() // R * (1 if dt != 3 else x.element_size())
+        arr_in = (C.c_void_p * R)(*[t.data_ptr() for t in ins])
+        arr_out = (C.c_void_p * R)(*[t.data_ptr() for t in outs])
+        rc = self._lib.lz_emu_all_to_all(self._emu, arr_in, arr_out, chunk, dt, int(compress), nblocks,
+                                         torch.cuda.current_stream().cuda_stream)
+        _native.check(rc, "emulated all_to_all")
+
     def broadcast_relay(self, src: int, dst_tensors, src_tensors, nblocks: int = 8):
         """Relay broadcast (peer stores) from emulated rank `src` into every
         rank's symmetric tensors dst_tensors[r] (lists from ``empty``)."""

@@ -12,21 +12,37 @@ KiB = 1 << 10
 MiB = 1 << 20
 
 # world -> list of (max_bytes, algo_with_multicast, algo_without_multicast).
-# 2 GPUs (sweep of 2xB200, bf16): one-shot wins up to 8 MB, two-shot above
-# (NVLS moves (1 + 1/N) S per GPU but is slower than two-shot's S at N = 2).
-# 8 GPUs: NVLS wins from 64 MB (621 vs 517 two-shot, NCCL 421) to 1 GB
-# (809 vs 646, NCCL 725).
-# Low-latency one-shot (flag-in-data pushes, no barrier) below 256 KB: 2xB200,
-# CUDA-graph device time, 1 KB 3.9 us and 256 KB 6.2 us vs NCCL 14.6 / 18.4 us.
+# Rows: (largest message in bytes, algorithm with NVLS multicast, without).
+# Fitted to CUDA-graph device times of the bf16 sweep on B200
+# (bench/allreduce_sweep.py --graph, max over ranks):
+#   2 GPUs: ll 3.9 us at 1 KB .. 6.2 us at 256 KB (NCCL 14.6 .. 18.4); one-shot
+#           up to 8 MB; two-shot above (NVLS moves (1 + 1/N) S per GPU, which
+#           at N = 2 is more than two-shot's S).
+#   4 GPUs: ll to 256 KB; one-shot to 2 MB; two-shot 4 MB .. 256 MB; NVLS from
+#           512 MB (1 GB: 2490 us vs NCCL 2523).
+#   8 GPUs: ll to 128 KB; one-shot to 512 KB; two-shot 1 .. 8 MB; NVLS from
+#           16 MB (1 GB: 2329 us vs NCCL 2595, 64 MB: 190 vs 278).
 TABLE = {
     2: [
         (256 * 1024, "ll", "ll"),
         (8 * MiB, "oneshot", "oneshot"),
         (1 << 62, "twoshot", "twoshot"),
     ],
-    "default": [
+    4: [
         (256 * 1024, "ll", "ll"),
-        (4 * MiB, "oneshot", "oneshot"),
+        (2 * MiB, "oneshot", "oneshot"),
+        (256 * MiB, "twoshot", "twoshot"),
+        (1 << 62, "nvls", "twoshot"),
+    ],
+    8: [
+        (128 * 1024, "ll", "ll"),
+        (512 * 1024, "oneshot", "oneshot"),
+        (8 * MiB, "twoshot", "twoshot"),
+        (1 << 62, "nvls", "twoshot"),
+    ],
+    "default": [
+        (128 * 1024, "ll", "ll"),
+        (1 * MiB, "oneshot", "oneshot"),
         (1 << 62, "nvls", "twoshot"),
     ],
 }
