@@ -99,3 +99,19 @@ def test_tg_record_api():
     assert rec.numel() % 16 == 0
     y = codec.tg_decode_cpu(rec, x.numel(), x.dtype)
     assert torch.equal(x.view(torch.int16), y.view(torch.int16))
+
+
+def test_decode_from_fixed_size_padded_buffer():
+    """A stream copied into a fixed-size message (the fixed-budget transfers
+    of the compressed ring) decodes from its prefix; trailing bytes of the
+    budget are ignored whatever they hold."""
+    from results_b200.ops import codec
+
+    torch.manual_seed(5)
+    x = (torch.randn(300_000) * 0.02).to(torch.bfloat16)
+    blob = codec.encode_cpu(x)
+    budget = blob.numel() + 4096
+    msg = torch.randint(0, 256, (budget,), dtype=torch.uint8)
+    msg[: blob.numel()] = blob
+    y = codec.decode_cpu(msg, x.numel(), x.dtype)
+    assert torch.equal(y.view(torch.int16), x.view(torch.int16))

@@ -92,3 +92,31 @@ def test_world8_ring_and_rhd():
                     timeout=300)
     bad = [r for rr in res for r in rr if not r[3]]
     assert not bad, bad
+
+
+def _pattern_worker(rank, world, nbytes, rounds):
+    import torch
+    import torch.distributed as dist
+
+    wrong = 0
+    for it in range(rounds):
+        if rank == 0:
+            buf = (torch.arange(nbytes, dtype=torch.int64) * 7 + it).remainder(251).to(torch.uint8)
+            reqs = [dist.isend(buf, dst=d) for d in range(1, world)]
+            for r in reqs:
+                r.wait()
+        else:
+            buf = torch.zeros(nbytes, dtype=torch.uint8)
+            dist.irecv(buf, src=0).wait()
+            want = (torch.arange(nbytes, dtype=torch.int64) * 7 + it).remainder(251).to(torch.uint8)
+            wrong += int((buf != want).sum().item())
+    return wrong
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_isend_irecv_fill_pattern_consistency(world):
+    """Point-to-point consistency (the reference's isend/irecv byte-pattern
+    test): rank 0 sends a position-dependent uint8 pattern to every other
+    rank, which counts wrong bytes; repeated rounds change the pattern."""
+    res = run_ranks(_pattern_worker, world, args=(3 << 20, 3))
+    assert res == [0] * world, res
