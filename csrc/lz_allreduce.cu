@@ -165,7 +165,7 @@ __device__ __forceinline__ void twoshot_body(const LzDevComm& c, const ArParams&
     Range rg = slice_piece(nv, W, p, G, b);
     size_t po = piece_offset_in_slice(nv, W, p, G, b);
     uint4* dst = reinterpret_cast<uint4*>(c.heap[p] + stage_off) + (size_t)me * slot_vecs + po;
-    copy_vecs<false>(dst, vin + rg.begin, rg.len);
+    if (lz_range_ok(c, dst, rg.len * 16, 25)) copy_vecs<false>(dst, vin + rg.begin, rg.len);
   }
   if (!block_barrier(c, epoch, 1)) return;
 
@@ -560,6 +560,7 @@ __device__ __forceinline__ void ll_oneshot_body(const LzDevComm& c, const ArPara
     for (int r = 0; r < LZ_MAX_RANKS; ++r) {
       if (r >= W || r == me) continue;
       char* dst = c.heap[r] + area + (size_t)me * slot + i * 32;
+      if (!lz_range_ok(c, dst, 32, 24)) continue;
       st_ll2(dst, w0, w1);
       st_ll2(dst + 16, w2, w3);
     }
@@ -677,6 +678,7 @@ static int init_comm_state(LzComm* c, int dev, size_t oneshot_bytes, size_t stag
   c->status_host = st_host;
   c->dev.status = st_dev;
   c->dev.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  c->dev.heap_bytes = c->heap_bytes;
   {
     const char* fa = getenv("LZ_FENCE_ALL");
     c->dev.fence_all = (fa && atoi(fa) != 0) ? 1 : 0;

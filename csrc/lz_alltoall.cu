@@ -76,13 +76,13 @@ __device__ __forceinline__ void a2a_body(const LzDevComm& c, const A2aParams& p)
     } else if (!kEnc) {
       char* tgt = zero_copy ? c.heap[dst] + p.out_off + (uint64_t)me * p.chunk_bytes
                             : c.heap[dst] + p.slot_off + (uint64_t)me * p.chunk_bytes;
-      cta_share_copy(tgt, src, p.chunk_bytes);
+      if (lz_range_ok(c, tgt, p.chunk_bytes, 22)) cta_share_copy(tgt, src, p.chunk_bytes);
     } else {
       A2aSmem& sm = *reinterpret_cast<A2aSmem*>(smem_raw);
       for (uint32_t t = b; t < p.ntg; t += G) {
         const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, p.chunk - (uint64_t)t * TG_ELEMS);
         char* rec = c.heap[dst] + p.slot_off + ((size_t)me * p.ntg + t) * p.cap;
-        encode_tg<DT>(src + (uint64_t)t * TG_ELEMS * ES, tn, rec, sm.enc);
+        if (lz_range_ok(c, rec, p.cap, 23)) encode_tg<DT>(src + (uint64_t)t * TG_ELEMS * ES, tn, rec, sm.enc);
       }
     }
   }

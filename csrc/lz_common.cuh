@@ -259,6 +259,29 @@ LZ_DEV bool lz_wait_ge(const LzDevComm& c, const unsigned long long* flag,
   return false;
 }
 
+#ifndef LZ_BOUNDS
+#define LZ_BOUNDS 0
+#endif
+// Debug builds (-DLZ_BOUNDS=1): a peer / multicast store range must lie in one
+// mapped heap; a violation is recorded (LZ_ERR_BOUNDS, `where`) and the caller
+// skips the store instead of executing it. Release builds compile this away.
+LZ_DEV bool lz_range_ok(const LzDevComm& c, const void* p, size_t len, int where) {
+#if LZ_BOUNDS
+  const char* q = static_cast<const char*>(p);
+  for (int r = 0; r < c.world; ++r)
+    if (q >= c.heap[r] && q + len <= c.heap[r] + c.heap_bytes) return true;
+  if (c.heap_mc && q >= c.heap_mc && q + len <= c.heap_mc + c.heap_bytes) return true;
+  lz_report(c, LZ_ERR_BOUNDS, where, 0);
+  return false;
+#else
+  (void)c;
+  (void)p;
+  (void)len;
+  (void)where;
+  return true;
+#endif
+}
+
 LZ_DEV unsigned long long flag_value(unsigned long long epoch, int phase) {
   return ((epoch + 1ull) << 3) | (unsigned long long)phase;
 }

@@ -31,6 +31,7 @@ struct LzDevComm {
   int* status;                    // host-mapped: first error (code | where)
   unsigned long long timeout_ns;  // bound of every flag wait
   int fence_all;                  // 1: every thread fences its peer stores before a signal
+  size_t heap_bytes;              // bytes of every rank's heap (bounds checks)
   int poll_relaxed;               // 1: flag polls are relaxed loads + one fence (default: ld.acquire)
 };
 

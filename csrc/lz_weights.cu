@@ -66,7 +66,8 @@ LZ_DEV int es_of(int dt) { return dt == LZ_F32 ? 4 : (dt == LZ_U8 ? 1 : 2); }  /
 // Byte copy of `bytes` from src to dst (16-B aligned both); the tail < 16 B is
 // assembled in a register and stored as one vector (dst capacity allows it).
 template <bool kMc>
-LZ_DEV void push_bytes(char* dst, const char* src, uint32_t bytes) {
+LZ_DEV void push_bytes(const LzDevComm& c, char* dst, const char* src, uint32_t bytes) {
+  if (!lz_range_ok(c, dst, (bytes + 15u) & ~15u, 20)) return;
   const uint32_t full = bytes & ~15u;
   constexpr int U = 8;  // loads in flight per thread
   uint32_t o = threadIdx.x * 16;
@@ -176,20 +177,21 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
         if (d.encode) {
           const bool direct = !p.use_mc && nrecv == 1;
           char* dst = direct ? c.heap[only] + slot_off : local;
+          if (!lz_range_ok(c, dst, p.cap, 21)) return;
           const uint32_t bytes = encode_dispatch(d.dtype, d.ptr, d.n, dst, sm.enc);
           if (p.use_mc) {
-            push_bytes<true>(c.heap_mc + slot_off, local, pad16(bytes));
+            push_bytes<true>(c, c.heap_mc + slot_off, local, pad16(bytes));
           } else if (!direct) {
             for (int r = 0; r < W; ++r)
-              if ((p.recv_mask >> r) & 1u) push_bytes<false>(c.heap[r] + slot_off, local, pad16(bytes));
+              if ((p.recv_mask >> r) & 1u) push_bytes<false>(c, c.heap[r] + slot_off, local, pad16(bytes));
           }
         } else {
           const uint32_t bytes = d.n * (uint32_t)es;
           if (p.use_mc) {
-            push_bytes<true>(c.heap_mc + slot_off, d.ptr, bytes);
+            push_bytes<true>(c, c.heap_mc + slot_off, d.ptr, bytes);
           } else {
             for (int r = 0; r < W; ++r)
-              if ((p.recv_mask >> r) & 1u) push_bytes<false>(c.heap[r] + slot_off, d.ptr, bytes);
+              if ((p.recv_mask >> r) & 1u) push_bytes<false>(c, c.heap[r] + slot_off, d.ptr, bytes);
           }
         }
       }
@@ -436,11 +438,11 @@ __global__ void __launch_bounds__(256) wx_direct_kernel(LzDevComm c, WxDirectPar
         const uint64_t off = ch * kDirectChunk;
         const uint32_t len = (uint32_t)min(kDirectChunk, d.bytes - off);
         if (p.use_mc) {
-          push_bytes<true>(c.heap_mc + d.dst_off + off, d.src + off, len);  // every rank, sender included
+          push_bytes<true>(c, c.heap_mc + d.dst_off + off, d.src + off, len);  // every rank, sender included
         } else {
           for (int r = 0; r < W; ++r)
             if (((p.recv_mask >> r) & 1u) || r == c.rank)
-              push_bytes<false>(c.heap[r] + d.dst_off + off, d.src + off, len);
+              push_bytes<false>(c, c.heap[r] + d.dst_off + off, d.src + off, len);
         }
       }
     }
@@ -553,7 +555,7 @@ LZ_DEV void relay_push_p2p(const LzDevComm& c, uint64_t off, const char* src, ui
     if (r == skip) continue;
     char* dst = c.heap[r] + off;
     if (dst == src) continue;
-    push_bytes<false>(dst, src, len);
+    push_bytes<false>(c, dst, src, len);
   }
 }
 
@@ -579,10 +581,10 @@ __device__ __forceinline__ void wx_relay_body(const LzDevComm& c, const WxRelayP
       const uint64_t hoff = d.dst_off + off;
       if (me == p.src) {
         if (owner == me) {
-          if (p.use_mc) push_bytes<true>(c.heap_mc + hoff, d.src + off, len);
+          if (p.use_mc) push_bytes<true>(c, c.heap_mc + hoff, d.src + off, len);
           else relay_push_p2p(c, hoff, d.src + off, len, -1);
         } else {
-          push_bytes<false>(c.heap[owner] + hoff, d.src + off, len);
+          push_bytes<false>(c, c.heap[owner] + hoff, d.src + off, len);
           publish_block_writes(c);
           if (threadIdx.x == 0) {
             unsigned long long* f = reinterpret_cast<unsigned long long*>(c.heap[owner] + rdy_off) + b;
@@ -597,7 +599,7 @@ __device__ __forceinline__ void wx_relay_body(const LzDevComm& c, const WxRelayP
         __syncthreads();
         if (s_fail) return;
         const char* mine = c.heap[me] + hoff;
-        if (p.use_mc) push_bytes<true>(c.heap_mc + hoff, mine, len);
+        if (p.use_mc) push_bytes<true>(c, c.heap_mc + hoff, mine, len);
         else relay_push_p2p(c, hoff, mine, len, me);
       }
     }

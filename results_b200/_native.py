@@ -57,7 +57,7 @@ def cuda():
         if _cuda_lib is None:
             from .utils import build
 
-            lib = _load("liblz_cuda.so", build.build_cuda)
+            lib = _load(build.cuda_lib_name(), build.build_cuda)
             _declare_cuda(lib)
             _cuda_lib = lib
     return _cuda_lib

@@ -62,6 +62,7 @@ class Config:
     pipeline_min_elements: int = 16 * 1024 * 1024
     # codec
     codec: str = "split_ans"          # "raw" | "split_ans"
+    ratio_budget: float = 0.65        # fixed-size budget of the host compressed ring / two-shot messages
     chunk_bytes: int = 64 * MiB       # pipelining unit of weight transfer / compressed paths
     # weight transfer
     update_weight_buffer_bytes: int = 512 * MiB
@@ -84,6 +85,7 @@ class Config:
             hd_max_bytes=_env_int("HD_MAX_MB", d.hd_max_bytes // MiB) * MiB,
             pipeline_min_elements=_env_int("LZ_PIPELINE_MIN_ELEMENTS", d.pipeline_min_elements),
             codec=_env_str("LZ_CODEC", d.codec),
+            ratio_budget=_env_float("LZ_RATIO_BUDGET", d.ratio_budget),
             chunk_bytes=_env_int("LZ_CHUNK_BYTES", d.chunk_bytes),
             update_weight_buffer_bytes=_env_int("LZ_UPDATE_WEIGHT_BUFFER_BYTES",
                                                 d.update_weight_buffer_bytes),

@@ -22,6 +22,7 @@ import torch
 
 from .. import _native, _native_sigs
 from ..utils.dtypes import LZ_BF16, LZ_F16, LZ_F32, LZ_U8
+from ..utils.trace import traced
 
 c_size, c_ptr, c_int, c_u64, c_u32 = C.c_size_t, C.c_void_p, C.c_int, C.c_uint64, C.c_uint32
 
@@ -157,6 +158,7 @@ def _stream_ptr(stream=None) -> int:
     return (stream or torch.cuda.current_stream()).cuda_stream
 
 
+@traced("encode")
 def encode(t: torch.Tensor, nblocks: int = 0, stream=None, return_size: bool = True):
     """Compress a contiguous CUDA tensor into a compact LZC1 stream.
 
@@ -182,6 +184,7 @@ def encode(t: torch.Tensor, nblocks: int = 0, stream=None, return_size: bool = T
     return out[: int(total.item())]
 
 
+@traced("decode")
 def decode(blob: torch.Tensor, like: torch.Tensor | None = None, n: int | None = None,
            dtype: torch.dtype | None = None, out: torch.Tensor | None = None, nblocks: int = 0,
            stream=None, check: bool = True) -> torch.Tensor:

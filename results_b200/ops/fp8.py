@@ -20,6 +20,7 @@ import math
 import torch
 
 from .. import _native, _native_sigs
+from ..utils.trace import traced
 
 _native_sigs.add_cuda({
     "lz_fp8_pack": (C.c_int, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_void_p),
@@ -37,6 +38,7 @@ def _kind(x_or_kind) -> int:
     return 0
 
 
+@traced("pack_fp8")
 def pack_fp8(x: torch.Tensor, kind: str | None = None) -> torch.Tensor:
     """fp8 (or uint8) tensor of even length -> uint16 containers (one per pair)."""
     k = KINDS[kind] if kind else _kind(x.dtype)
@@ -54,6 +56,7 @@ def pack_fp8(x: torch.Tensor, kind: str | None = None) -> torch.Tensor:
     return out
 
 
+@traced("unpack_fp8")
 def unpack_fp8(w: torch.Tensor, kind: str = "e4m3", dtype: torch.dtype | None = None) -> torch.Tensor:
     """uint16 containers -> fp8 bytes (viewed as `dtype` when given)."""
     k = KINDS[kind]

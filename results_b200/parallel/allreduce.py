@@ -20,6 +20,7 @@ import torch
 import torch.distributed as dist
 
 from ..config import Config
+from ..utils.trace import traced
 from .comm import Communicator
 
 _DEFAULT: Communicator | None = None
@@ -56,6 +57,7 @@ def select_algo(nbytes: int, world: int, has_multicast: bool, symmetric: bool,
     return choose(nbytes, world, has_multicast, symmetric)
 
 
+@traced("allreduce")
 def allreduce(t: torch.Tensor, algo: str = "auto", out: torch.Tensor | None = None,
               comm: Communicator | None = None, group=None) -> torch.Tensor:
     """Sum-allreduce ``t`` across the group. In place unless ``out`` is given."""

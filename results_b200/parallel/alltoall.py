@@ -23,6 +23,7 @@ import torch.distributed as dist
 
 from .. import _native, _native_sigs
 from ..utils.dtypes import lz_dtype
+from ..utils.trace import traced
 
 _native_sigs.add_cuda({
     "lz_all_to_all": (C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_int,
@@ -40,6 +41,7 @@ def stage_bytes_needed(numel: int, dtype: torch.dtype, world: int, compress: boo
     return _native.cuda().lz_all_to_all_stage_bytes(numel // world, lz_dtype(dtype), world, int(compress))
 
 
+@traced("all_to_all")
 def all_to_all(x: torch.Tensor, out: torch.Tensor | None = None, compress: bool = False, comm=None,
                nblocks: int = 0, stream=None) -> torch.Tensor:
     """Exchange equal chunks: chunk j of every rank's ``x`` lands as chunk

@@ -36,6 +36,7 @@ import torch.distributed as dist
 from .. import _native, _native_sigs
 from ..ops import codec
 from ..utils.dtypes import lz_dtype
+from ..utils.trace import traced
 
 _native_sigs.add_cuda({
     "lz_cz_stage_bytes": (C.c_size_t, C.c_size_t, C.c_int, C.c_int, C.c_int),
@@ -54,6 +55,7 @@ def stage_bytes_needed(n: int, dtype: torch.dtype, world: int, nblocks: int = 44
     return int(_native.cuda().lz_cz_stage_bytes(n, lz_dtype(dtype), world, nblocks))
 
 
+@traced("compressed_allreduce")
 def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=None,
                          nblocks: int = 0, multicast: bool = True, stream=None) -> torch.Tensor:
     """Sum-allreduce with lossless compression on the wire (native fused kernel)."""
@@ -73,10 +75,12 @@ def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=
 
 
 # ----------------------------------------------------------------------------- messages
+@traced("compress")
 def _encode(x: torch.Tensor) -> torch.Tensor:
     return codec.encode(x) if x.is_cuda else codec.encode_cpu(x)
 
 
+@traced("decompress")
 def _decode(blob: torch.Tensor, n: int, dtype, out: torch.Tensor | None = None) -> torch.Tensor:
     y = codec.decode(blob, n=n, dtype=dtype) if blob.is_cuda else codec.decode_cpu(blob, n, dtype)
     if out is not None:
@@ -123,6 +127,7 @@ class _Stats:
 STATS = _Stats()
 
 
+@traced("exchange")
 def _exchange_compressed(pairs, group, budget):
     """pairs: list of (peer, blob_to_send, (n, dtype, out_or_None)) -> decoded list.
 
@@ -235,6 +240,7 @@ def compressed_ring(t: torch.Tensor, group=None, ratio: float = 0.65) -> torch.T
     return t
 
 
+@traced("ring_hop")
 def _ring_hop(blob, right, left, group, budget, n_recv, dtype):
     msg, rest = _pack(blob, budget)
     r = torch.empty(budget, dtype=torch.uint8, device=blob.device)

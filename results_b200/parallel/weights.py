@@ -32,6 +32,7 @@ import torch.distributed as dist
 
 from .. import _native, _native_sigs
 from ..ops import codec
+from ..utils import trace
 
 _native_sigs.add_cuda({
     "lz_wx_slot_capacity": (C.c_size_t,),
@@ -271,15 +272,34 @@ def _engine(comm, mode, **kw):
     return cache[key]
 
 
+def _progress(items, what: str):
+    """tqdm progress over buckets when LZ_PROGRESS=1 (tqdm is optional)."""
+    if os.environ.get("LZ_PROGRESS", "0") in ("", "0"):
+        return items
+    try:
+        from tqdm import tqdm
+    except ImportError:
+        return items
+    return tqdm(items, desc=what, unit="bucket")
+
+
+def _log_bucket(what: str, i: int, bucket) -> None:
+    nbytes = sum(t.numel() * t.element_size() for _, t in bucket)
+    trace.log.info("[BUCKET] %s %d start tensors=%d bytes=%.1fMB", what, i, len(bucket), nbytes / 2**20)
+
+
 def send_weights(state_dict, dst, comm=None, mode: str = "split_ans", bucket_bytes: int | None = None,
                  dump_dir: str | None = None, weight_version: int = 0, **kw) -> None:
     """Send a state_dict (name -> CUDA tensor) to rank(s) `dst`, bucket by bucket."""
     eng = _engine(comm, mode, **kw)
     bb = bucket_bytes or eng.comm.config.update_weight_buffer_bytes
-    for i, bucket in enumerate(buckets(list(state_dict.items()), bb)):
+    trace.log.info("[START] send_weights version=%d mode=%s dst=%s", weight_version, mode, dst)
+    for i, bucket in enumerate(_progress(list(buckets(list(state_dict.items()), bb)), "send_weights")):
+        _log_bucket("send", i, bucket)
         if dump_dir:
             dump_tensors(bucket, dump_dir, weight_version, i, group_name=f"src{eng.comm.rank}")
-        eng.send([t for _, t in bucket], dst)
+        with trace.range(f"send_weights.bucket{i}"):
+            eng.send([t for _, t in bucket], dst)
 
 
 def recv_weights(state_dict, src: int, comm=None, mode: str = "split_ans", bucket_bytes: int | None = None,
@@ -287,8 +307,10 @@ def recv_weights(state_dict, src: int, comm=None, mode: str = "split_ans", bucke
     """Receive into the destination tensors of `state_dict` (same names, shapes, order)."""
     eng = _engine(comm, mode, **kw)
     bb = bucket_bytes or eng.comm.config.update_weight_buffer_bytes
-    for bucket in buckets(list(state_dict.items()), bb):
-        eng.recv([t for _, t in bucket], src)
+    for i, bucket in enumerate(_progress(list(buckets(list(state_dict.items()), bb)), "recv_weights")):
+        _log_bucket("recv", i, bucket)
+        with trace.range(f"recv_weights.bucket{i}"):
+            eng.recv([t for _, t in bucket], src)
     return state_dict
 
 
@@ -296,8 +318,10 @@ def broadcast_weights(state_dict, src: int = 0, comm=None, mode: str = "split_an
                       bucket_bytes: int | None = None, **kw) -> dict:
     eng = _engine(comm, mode, **kw)
     bb = bucket_bytes or eng.comm.config.update_weight_buffer_bytes
-    for bucket in buckets(list(state_dict.items()), bb):
-        eng.broadcast([t for _, t in bucket], src)
+    for i, bucket in enumerate(_progress(list(buckets(list(state_dict.items()), bb)), "broadcast_weights")):
+        _log_bucket("broadcast", i, bucket)
+        with trace.range(f"broadcast_weights.bucket{i}"):
+            eng.broadcast([t for _, t in bucket], src)
     return state_dict
 
 

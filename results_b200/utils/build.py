@@ -83,23 +83,45 @@ def build_cpu(force: bool = False) -> Path:
     return CPU_LIB
 
 
-def build_cuda(force: bool = False, jobs: int | None = None, ptxas_verbose: bool = False) -> Path:
+def bounds_requested() -> bool:
+    """LZ_BOUNDS=1 selects the range-checked debug build of the CUDA library."""
+    return os.environ.get("LZ_BOUNDS", "0") not in ("", "0")
+
+
+def cuda_lib_name(bounds: bool | None = None) -> str:
+    return "liblz_cuda_bounds.so" if (bounds_requested() if bounds is None else bounds) else "liblz_cuda.so"
+
+
+def build_cuda(force: bool = False, jobs: int | None = None, ptxas_verbose: bool = False,
+               bounds: bool | None = None) -> Path:
+    """Compile every csrc/*.cu for sm_100a and link the runtime library.
+
+    ``bounds`` (default: environment LZ_BOUNDS) builds the debug variant with
+    -DLZ_BOUNDS=1 into ``liblz_cuda_bounds.so``: every peer / multicast store
+    range is checked against the mapped heaps and a violation is recorded in
+    the status word (code 3, bounds) instead of being executed.
+    """
     if not Path(NVCC).exists():
         raise RuntimeError(f"nvcc not found at {NVCC}")
+    bounds = bounds_requested() if bounds is None else bounds
     srcs = cuda_sources()
     hdr_time = _newest(_headers())
-    OBJ_DIR.mkdir(parents=True, exist_ok=True)
+    obj_dir = OBJ_DIR.with_name(OBJ_DIR.name + "_bounds") if bounds else OBJ_DIR
+    lib = LIB_DIR / cuda_lib_name(bounds)
+    obj_dir.mkdir(parents=True, exist_ok=True)
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     objs = []
     todo = []
     for s in srcs:
-        o = OBJ_DIR / (s.name + ".o")
+        o = obj_dir / (s.name + ".o")
         objs.append(o)
         if force or not o.exists() or o.stat().st_mtime < max(s.stat().st_mtime, hdr_time):
             todo.append((s, o))
     flags = list(NVCC_FLAGS)
     if ptxas_verbose:
         flags += ["-Xptxas", "-v"]
+    if bounds:
+        flags += ["-DLZ_BOUNDS=1"]
 
     def compile_one(so):
         s, o = so
@@ -110,12 +132,12 @@ def build_cuda(force: bool = False, jobs: int | None = None, ptxas_verbose: bool
     jobs = jobs or min(len(todo) or 1, os.cpu_count() or 4)
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
         list(ex.map(compile_one, todo))
-    if todo or force or not CUDA_LIB.exists() or CUDA_LIB.stat().st_mtime < _newest(objs):
-        tmp = CUDA_LIB.with_suffix(f".so.tmp{os.getpid()}")
+    if todo or force or not lib.exists() or lib.stat().st_mtime < _newest(objs):
+        tmp = lib.with_suffix(f".so.tmp{os.getpid()}")
         _run([NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(tmp),
               "-lpthread", "-ldl", "-lrt"])
-        os.replace(tmp, CUDA_LIB)
-    return CUDA_LIB
+        os.replace(tmp, lib)
+    return lib
 
 
 def build_all(force: bool = False) -> tuple[Path, Path]:

@@ -57,3 +57,32 @@ def test_config_env(monkeypatch):
 
 def test_size_labels():
     assert csvfmt.size_label(1 << 30) == "1 GB" and csvfmt.size_label(1024) == "1 KB"
+
+
+def test_trace_ranges_and_bucket_logs(caplog):
+    """Tracing is a no-op unless enabled; enabled ranges nest without a GPU
+    profiler attached; bucket log lines carry tensor and byte counts."""
+    import logging
+
+    import torch
+
+    from results_b200.parallel import weights
+    from results_b200.utils import trace
+
+    calls = []
+
+    @trace.traced("probe")
+    def f(x, algo=None):
+        calls.append(x)
+        return x + 1
+
+    assert f(1) == 2
+    trace.enable(True)
+    try:
+        if torch.cuda.is_available():
+            assert f(2, algo="ll") == 3
+    finally:
+        trace.enable(False)
+    with caplog.at_level(logging.INFO, logger="results_b200"):
+        weights._log_bucket("send", 3, [("a", torch.zeros(1024)), ("b", torch.zeros(256, dtype=torch.bfloat16))])
+    assert any("[BUCKET] send 3 start tensors=2" in r.getMessage() for r in caplog.records)
