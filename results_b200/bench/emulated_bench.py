@@ -1,6 +1,7 @@
 """Single-GPU timing of the multi-rank kernel bodies through the R-rank emulator.
 
     python -m results_b200.bench.emulated_bench --world 8 --mb 256 --algos oneshot,twoshot,compressed
+    (also: ll, a2a_raw, a2a_compressed, relay, wx_raw, wx_split)
 
 Every emulated rank's heap lives on one GPU and the collective runs as one
 cooperative launch, so the numbers measure the kernel bodies (barriers,
@@ -64,12 +65,28 @@ def main(argv=None):
         if algo == "oneshot" and n * es > oneshot:
             print(json.dumps({"algo": algo, "skipped": f"one-shot is limited to {oneshot} bytes"}), flush=True)
             continue
+        if algo == "ll" and n * es > 256 * 1024:
+            print(json.dumps({"algo": algo, "skipped": "ll is limited to 256 KB"}), flush=True)
+            continue
+        check = True
         if algo == "compressed":
             fn = lambda: w.compressed_allreduce(ins, outs, nblocks=args.nblocks)  # noqa: E731
+        elif algo in ("a2a_raw", "a2a_compressed"):
+            fn = lambda c=(algo == "a2a_compressed"): w.all_to_all(ins, outs, compress=c,  # noqa: E731
+                                                                   nblocks=args.nblocks)
+            check = False
+        elif algo == "relay":
+            fn = lambda: w.broadcast_relay(0, [[o] for o in outs], [ins[0]], nblocks=ar_blocks)  # noqa: E731
+            check = False
+        elif algo in ("wx_raw", "wx_split"):
+            fn = lambda e=(algo == "wx_split"): w.weight_transfer(  # noqa: E731
+                0, list(range(1, R)), [[ins[0]]] + [[o] for o in outs[1:]], encode=e, nblocks=ar_blocks,
+                broadcast_all=True)
+            check = False
         else:
             fn = lambda a=algo: w.allreduce(ins, outs, algo=a, nblocks=ar_blocks)  # noqa: E731
         ms = _time(fn, args.iters, args.warmup)
-        err = (outs[0].float() - ref).abs().max().item()
+        err = (outs[0].float() - ref).abs().max().item() if check else None
         # HBM bytes per rank of the emulated collective (every "peer" access
         # is local): one-shot = copy-in (2n) + R reads and one write of n;
         # two-shot = input read + push (2n) + reduce read n and 2n/R writes +
