@@ -38,6 +38,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--world", type=int, default=8)
     ap.add_argument("--mb", type=int, default=256, help="per-rank message size in MiB")
+    ap.add_argument("--kb", type=int, default=0, help="per-rank message size in KiB (overrides --mb)")
     ap.add_argument("--algos", default="oneshot,twoshot,compressed")
     ap.add_argument("--dtype", default="bfloat16")
     ap.add_argument("--iters", type=int, default=5)
@@ -46,7 +47,7 @@ def main(argv=None):
     args = ap.parse_args(argv)
     dt = getattr(torch, args.dtype)
     es = torch.empty((), dtype=dt).element_size()
-    n = (args.mb << 20) // es
+    n = ((args.kb << 10) if args.kb else (args.mb << 20)) // es
     R = args.world
     oneshot = min(n * es, 8 << 20)
     stage = max(64 << 20, 2 * n * es + (96 << 20))
