@@ -316,7 +316,20 @@ def recv_weights(state_dict, src: int, comm=None, mode: str = "split_ans", bucke
 
 def broadcast_weights(state_dict, src: int = 0, comm=None, mode: str = "split_ans",
                       bucket_bytes: int | None = None, **kw) -> dict:
+    """Every rank calls: `src` sends its state_dict, the others receive into theirs.
+
+    With ``mode="raw"`` and every tensor allocated in the symmetric heap
+    (``comm.empty``, same order on all ranks) the update goes zero-copy
+    through :meth:`WeightTransfer.broadcast_direct` (relay broadcast for more
+    than two ranks): no slots and no receiver copies, in one launch.
+    """
     eng = _engine(comm, mode, **kw)
+    tensors = list(state_dict.values())
+    if mode == "raw" and tensors and all(t.is_cuda and eng.comm.is_symmetric(t) for t in tensors):
+        trace.log.info("[START] broadcast_weights zero-copy tensors=%d src=%d", len(tensors), src)
+        with trace.range("broadcast_weights.direct"):
+            eng.broadcast_direct(tensors, src)
+        return state_dict
     bb = bucket_bytes or eng.comm.config.update_weight_buffer_bytes
     for i, bucket in enumerate(_progress(list(buckets(list(state_dict.items()), bb)), "broadcast_weights")):
         _log_bucket("broadcast", i, bucket)

@@ -67,6 +67,18 @@ def _worker(rank, world, cases, dump_dir):
                 f"numel {a.numel()} first diff at {first} got {int(a[first])} want {int(b[first])} "
                 f"ptr%16={sym[bad_idx[0]].data_ptr() % 16}")
     results.append(("raw", "direct", diag, not bad_idx))
+    # public API: broadcast_weights of a symmetric state_dict takes the zero-copy path
+    sym_sd = {k: comm.empty(t.shape, t.dtype) for k, t in ref.items()}
+    for k, t in sym_sd.items():
+        if rank == 0:
+            t.copy_(ref[k])
+        else:
+            t.fill_(-5)
+    weights.broadcast_weights(sym_sd, 0, comm=comm, mode="raw")
+    torch.cuda.synchronize()
+    comm.check()
+    results.append(("raw", "broadcast_weights_symmetric", 0.0,
+                    all(torch.equal(sym_sd[k].view(torch.int16), ref[k].view(torch.int16)) for k in ref)))
     # dump oracle: rank 0 dumps, the others compare what they received with it
     if rank == 0:
         weights.dump_tensors(list(ref.items()), dump_dir, 3, 0, group_name="test")
