@@ -155,8 +155,14 @@ def main(argv=None):
                               f"exact={exact}", flush=True)
             if a.fp8 and world >= 2:
                 eng = weights.WeightTransfer(comm, mode="split_ans")
+                x0 = _data(n, kind, 900) if rank == 1 else x  # the sender's (rank 0's) tensor
+
+                def cast(t, f8):
+                    return t.float().clamp(-448, 448).to(f8) if f8 == torch.float8_e4m3fn else t.to(f8)
+
                 for f8 in (torch.float8_e4m3fn, torch.float8_e5m2):
-                    xf = x.float().clamp(-448, 448).to(f8) if f8 == torch.float8_e4m3fn else x.to(f8)
+                    xf = cast(x, f8)
+                    want = cast(x0, f8)
                     dst = torch.empty_like(xf) if rank == 1 else xf
                     fratio = _max(codec.compression_ratio(xf), ctrl)
 
@@ -167,7 +173,7 @@ def main(argv=None):
                             eng.recv([dst], 0)
 
                     ms = timed(send, None)
-                    exact = bool(torch.equal(dst.view(torch.uint8), xf.view(torch.uint8))) if rank == 1 else True
+                    exact = bool(torch.equal(dst.view(torch.uint8), want.view(torch.uint8))) if rank == 1 else True
                     ok = torch.tensor([0 if exact else 1])
                     dist.all_reduce(ok, group=ctrl)
                     fb = xf.numel()
