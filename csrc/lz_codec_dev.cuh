@@ -223,7 +223,7 @@ LZ_DEV void build_tables_warp0(EncSmem& sm, uint32_t n) {
     c[k] = sm.hist[s];
     f[k] = 0;
     if (c[k]) {
-      f[k] = (uint32_t)(((uint64_t)c[k] * PROB_SCALE) / n);
+      f[k] = (c[k] * PROB_SCALE) / n;  // c <= n <= 32768: the product fits 32 bits
       if (f[k] == 0) f[k] = 1;
       if (c[k] > maxc) {
         maxc = c[k];
@@ -301,6 +301,47 @@ LZ_DEV void build_tables_warp0(EncSmem& sm, uint32_t n) {
     cum += f[k];
   }
   if (lane == 31) sm.nnz = inz;
+}
+
+// ---------------------------------------------------------------------------
+// Interleaved rANS of one sub-block (sn <= SUB_ELEMS symbols at sm.syms[base])
+// by one warp, backward over the steps: lane l owns symbols l, l+32, ...;
+// renormalisation words of a step are written in lane order after the 128-byte
+// state area. Returns false when the words would not beat the raw bytes.
+// kFull: sn == SUB_ELEMS, so every step has all 32 lanes active.
+// ---------------------------------------------------------------------------
+template <bool kFull>
+LZ_DEV bool rans_encode_sub(EncSmem& sm, uint32_t base, uint32_t sn, uint32_t warp, uint32_t lane,
+                            uint32_t& x_out, uint32_t& pos_out) {
+  if (sn < 128u) return false;  // the 32 states alone do not beat the raw bytes
+  uint16_t* words = reinterpret_cast<uint16_t*>(sm.u.streams[warp] + 128);
+  const uint32_t lim = (sn - 128u) / 2u;  // words that still beat the raw bytes
+  uint32_t x = RANS_L;
+  uint32_t pos = 0;  // words emitted (warp-uniform)
+  const int jmax = (int)((sn + LANES - 1) / LANES) - 1;
+  const uint32_t lt = lanemask_lt();
+  const uint8_t* syms = sm.syms + base + lane;
+  // software-pipelined: the table entry of step j-1 is fetched while step j runs
+  EncSym e_next;
+  if (kFull || (uint32_t)jmax * LANES + lane < sn) e_next = sm.tab[syms[(uint32_t)jmax * LANES]];
+  for (int j = jmax; j >= 0; --j) {
+    const bool act = kFull || (uint32_t)j * LANES + lane < sn;
+    const EncSym e = e_next;
+    if (j > 0) e_next = sm.tab[syms[(uint32_t)(j - 1) * LANES]];
+    const bool need = act && enc_needs_word(x, e.freq);
+    const uint32_t m = __ballot_sync(0xffffffffu, need);
+    const uint32_t cnt = __popc(m);
+    if (pos + cnt > lim) return false;
+    if (need) {
+      words[pos + __popc(m & lt)] = (uint16_t)(x & 0xFFFF);
+      x >>= 16;
+    }
+    pos += cnt;
+    if (act) x = enc_update(x, e);
+  }
+  x_out = x;
+  pos_out = pos;
+  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -391,44 +432,18 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
   if (warp < nsub) {
     const uint32_t base = warp * SUB_ELEMS;
     const uint32_t sn = min(SUB_ELEMS, n - base);
+    uint32_t x, pos;
+    // full sub-blocks (every step has 32 symbols) take the branch-free loop
+    const bool ok = sn == SUB_ELEMS ? rans_encode_sub<true>(sm, base, sn, warp, lane, x, pos)
+                                    : rans_encode_sub<false>(sm, base, sn, warp, lane, x, pos);
     uint8_t* out = sm.u.streams[warp];
-    uint32_t x = RANS_L;
-    uint32_t pos = 0;  // words emitted (warp-uniform)
-    bool overflow = false;
-    const int jmax = (int)((sn + LANES - 1) / LANES) - 1;
-    const uint32_t lt = lanemask_lt();
-    // software-pipelined: the table entry of step j-1 is fetched while step j runs
-    EncSym e_next;
-    {
-      const uint32_t i0 = (uint32_t)jmax * LANES + lane;
-      if (jmax >= 0 && i0 < sn) e_next = sm.tab[sm.syms[base + i0]];
-    }
-    for (int j = jmax; j >= 0; --j) {
-      const uint32_t i = (uint32_t)j * LANES + lane;
-      const bool act = i < sn;
-      const EncSym e = e_next;
-      if (j > 0) e_next = sm.tab[sm.syms[base + i - LANES]];
-      const bool need = act && enc_needs_word(x, e.freq);
-      const uint32_t m = __ballot_sync(0xffffffffu, need);
-      const uint32_t cnt = __popc(m);
-      if (128u + 2u * (pos + cnt) > sn) {
-        overflow = true;
-        break;
-      }
-      if (need) {
-        *reinterpret_cast<uint16_t*>(out + 128 + 2 * (pos + __popc(m & lt))) = (uint16_t)(x & 0xFFFF);
-        x >>= 16;
-      }
-      pos += cnt;
-      if (act) x = enc_update(x, e);
-    }
-    if (!overflow) {
+    if (ok) {
       reinterpret_cast<uint32_t*>(out)[lane] = x;
       // zero the padding words so records are deterministic
       const uint32_t len = 128u + 2u * pos;
       if (lane < (pad16(len) - len) / 2) *reinterpret_cast<uint16_t*>(out + len + 2 * lane) = 0;
     }
-    if (lane == 0) sm.sub_len[warp] = overflow ? 0u : 128u + 2u * pos;
+    if (lane == 0) sm.sub_len[warp] = ok ? 128u + 2u * pos : 0u;
   }
   __syncthreads();
   if (stop_after == 3) return 0;

@@ -235,8 +235,11 @@ LZC_HD uint32_t umulhi32(uint32_t a, uint32_t b) {
 
 // One rANS encode step: returns true (and the word) if a renormalisation word
 // must be emitted before the state update.
+// x >= f << (32 - PROB_BITS), evaluated in 32 bits: the shifted bound has no
+// low bits, so comparing x's top PROB_BITS+1 bits with f is equivalent (and
+// f = PROB_SCALE, a single-symbol table, never renormalises).
 LZC_HD bool enc_needs_word(uint32_t x, uint32_t f) {
-  return (uint64_t)x >= ((uint64_t)f << (32 - PROB_BITS));
+  return (x >> (32 - PROB_BITS)) >= f;
 }
 LZC_HD uint32_t enc_update(uint32_t x, const EncSym& e) {
   const uint32_t q = (uint32_t)(((uint64_t)x + umulhi32(x, e.m_lo)) >> e.shift);
