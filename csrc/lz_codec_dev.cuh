@@ -212,6 +212,34 @@ LZ_DEV void cta_copy16(char* dst, const char* src, uint32_t bytes) {
 // Frequency table (warp 0): counts -> freq -> cumulative -> encoder table and
 // the compact list of (sym << 16 | freq). Same result as normalize_freqs().
 // ---------------------------------------------------------------------------
+// Reciprocals of every frequency 1..PROB_SCALE, built at compile time with
+// the same formula as make_enc_sym (so the entries are identical): the table
+// build then loads them instead of running a 64-bit division per symbol.
+struct RcpTable {
+  uint32_t m_lo[PROB_SCALE + 1];
+  uint8_t shift[PROB_SCALE + 1];
+};
+constexpr RcpTable make_rcp_table() {
+  RcpTable t{};
+  for (uint32_t f = 1; f <= PROB_SCALE; ++f) {
+    uint32_t l = 0;
+    while ((1u << l) < f) ++l;
+    t.shift[f] = (uint8_t)l;
+    t.m_lo[f] = (uint32_t)((((uint64_t)1 << (32 + l)) + f - 1) / f - ((uint64_t)1 << 32));
+  }
+  return t;
+}
+__device__ constexpr RcpTable kRcp = make_rcp_table();
+
+LZ_DEV EncSym enc_sym_from_table(uint32_t f, uint32_t cum) {
+  EncSym e;
+  e.freq = f;
+  e.cum = cum;
+  e.shift = kRcp.shift[f];
+  e.m_lo = kRcp.m_lo[f];
+  return e;
+}
+
 LZ_DEV void build_tables_warp0(EncSmem& sm, uint32_t n) {
   const uint32_t lane = lane_id();
   uint32_t c[8], f[8];
@@ -223,7 +251,8 @@ LZ_DEV void build_tables_warp0(EncSmem& sm, uint32_t n) {
     c[k] = sm.hist[s];
     f[k] = 0;
     if (c[k]) {
-      f[k] = (c[k] * PROB_SCALE) / n;  // c <= n <= 32768: the product fits 32 bits
+      // c <= n <= 32768: the product fits 32 bits; a full TG divides by 2^15
+      f[k] = (n & (n - 1)) == 0 ? (c[k] * PROB_SCALE) >> (31 - __clz(n)) : (c[k] * PROB_SCALE) / n;
       if (f[k] == 0) f[k] = 1;
       if (c[k] > maxc) {
         maxc = c[k];
@@ -295,7 +324,7 @@ LZ_DEV void build_tables_warp0(EncSmem& sm, uint32_t n) {
   for (int k = 0; k < 8; ++k) {
     const int s = lane * 8 + k;
     if (f[k]) {
-      sm.tab[s] = make_enc_sym(f[k], cum);
+      sm.tab[s] = enc_sym_from_table(f[k], cum);
       sm.table[pos++] = ((uint32_t)s << 16) | f[k];
     }
     cum += f[k];
@@ -503,6 +532,44 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
 }
 
 // ---------------------------------------------------------------------------
+// Interleaved rANS decode of one sub-stream (`len` bytes at `st`: 32 states,
+// then 16-bit words) into sm.syms[base, base + sn) by one warp, forward over
+// the steps (the encoder's words are consumed in reverse). Returns true when
+// every word was consumed and every lane ended in the initial state.
+// kFull: sn == SUB_ELEMS, so every step has all 32 lanes active.
+// ---------------------------------------------------------------------------
+template <bool kFull>
+LZ_DEV bool rans_decode_sub(DecSmem& sm, const char* st, uint32_t len, uint32_t base, uint32_t sn,
+                            uint32_t lane) {
+  uint32_t x = *reinterpret_cast<const uint32_t*>(st + 4 * lane);
+  const uint16_t* words = reinterpret_cast<const uint16_t*>(st + 128);
+  int E = (int)((len - 128) / 2);
+  const uint32_t lt = lanemask_lt();
+  const int jn = (int)((sn + LANES - 1) / LANES);
+  uint8_t* syms = sm.syms + base + lane;
+  bool wok = true;
+  for (int j = 0; j < jn; ++j) {
+    const bool act = kFull || (uint32_t)j * LANES + lane < sn;
+    bool need = false;
+    if (act) {
+      const uint32_t ent = sm.dtab[x & (PROB_SCALE - 1)];
+      syms[(uint32_t)j * LANES] = (uint8_t)(ent & 0xFF);
+      x = dec_update(x, ent);
+      need = x < RANS_L;
+    }
+    const uint32_t m = __ballot_sync(0xffffffffu, need);
+    const int k = __popc(m);
+    if (k > E) {
+      wok = false;
+      break;
+    }
+    if (need) x = (x << 16) | words[E - k + __popc(m & lt)];
+    E -= k;
+  }
+  return wok && E == 0 && x == RANS_L;
+}
+
+// ---------------------------------------------------------------------------
 // Decode the symbol plane of the TG record at `src` (n elements expected)
 // into sm.syms. Returns true on success (uniform over the CTA); the raw plane
 // starts at src + sizeof(TgHeader). A corrupt record returns false.
@@ -617,32 +684,9 @@ LZ_DEV bool decode_tg_syms(const char* __restrict__ src, uint32_t cap, uint32_t 
         const char* st = symsec + off;
         const uint32_t base = b * SUB_ELEMS;
         const uint32_t sn = min(SUB_ELEMS, n - base);
-        uint32_t x = *reinterpret_cast<const uint32_t*>(st + 4 * lane);
-        const uint16_t* words = reinterpret_cast<const uint16_t*>(st + 128);
-        int E = (int)((len - 128) / 2);
-        const uint32_t lt = lanemask_lt();
-        const int jn = (int)((sn + LANES - 1) / LANES);
-        bool wok = true;
-        for (int j = 0; j < jn; ++j) {
-          const uint32_t i = (uint32_t)j * LANES + lane;
-          const bool act = i < sn;
-          bool need = false;
-          if (act) {
-            const uint32_t ent = sm.dtab[x & (PROB_SCALE - 1)];
-            sm.syms[base + i] = (uint8_t)(ent & 0xFF);
-            x = dec_update(x, ent);
-            need = x < RANS_L;
-          }
-          const uint32_t m = __ballot_sync(0xffffffffu, need);
-          const int k = __popc(m);
-          if (k > E) {
-            wok = false;
-            break;
-          }
-          if (need) x = (x << 16) | words[E - k + __popc(m & lt)];
-          E -= k;
-        }
-        wok = wok && E == 0 && x == RANS_L;
+        // full sub-streams (every step has 32 symbols) take the branch-free loop
+        bool wok = sn == SUB_ELEMS ? rans_decode_sub<true>(sm, st, len, base, sn, lane)
+                                   : rans_decode_sub<false>(sm, st, len, base, sn, lane);
         wok = __all_sync(0xffffffffu, wok);
         if (!wok && lane == 0) sm.ok = 0;
       }
