@@ -91,24 +91,34 @@ struct Split16<DT_F16> {
 };
 template <>
 struct Split16<DT_F32> {
+  // raw plane: 3 little-endian bytes per element; four elements' 24-bit raws
+  // fill three 32-bit words exactly (r0 | r1 << 24, r1 >> 8 | r2 << 16,
+  // r2 >> 16 | r3 << 8), so the packing is done with word shifts
   static constexpr int IN_VECS = 4, RAW_BYTES = 48;
   LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t* raw) {
     const uint32_t* w = reinterpret_cast<const uint32_t*>(v);
+    uint32_t* rw = reinterpret_cast<uint32_t*>(raw);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      sym[k] = sym_f32(w[k]);
-      const uint32_t r = raw_f32(w[k]);
-      raw[3 * k] = (uint8_t)r;
-      raw[3 * k + 1] = (uint8_t)(r >> 8);
-      raw[3 * k + 2] = (uint8_t)(r >> 16);
+    for (int k = 0; k < 16; ++k) sym[k] = sym_f32(w[k]);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint32_t r0 = raw_f32(w[4 * g]), r1 = raw_f32(w[4 * g + 1]);
+      const uint32_t r2 = raw_f32(w[4 * g + 2]), r3 = raw_f32(w[4 * g + 3]);
+      rw[3 * g] = r0 | (r1 << 24);
+      rw[3 * g + 1] = (r1 >> 8) | (r2 << 16);
+      rw[3 * g + 2] = (r2 >> 16) | (r3 << 8);
     }
   }
   LZ_DEV static void merge(const uint8_t* sym, const uint8_t* raw, uint4* v) {
     uint32_t* w = reinterpret_cast<uint32_t*>(v);
+    const uint32_t* rw = reinterpret_cast<const uint32_t*>(raw);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const uint32_t r = raw[3 * k] | ((uint32_t)raw[3 * k + 1] << 8) | ((uint32_t)raw[3 * k + 2] << 16);
-      w[k] = merge_f32(sym[k], r);
+    for (int g = 0; g < 4; ++g) {
+      const uint32_t a = rw[3 * g], b = rw[3 * g + 1], c = rw[3 * g + 2];
+      w[4 * g] = merge_f32(sym[4 * g], a & 0xFFFFFFu);
+      w[4 * g + 1] = merge_f32(sym[4 * g + 1], (a >> 24) | ((b & 0xFFFFu) << 8));
+      w[4 * g + 2] = merge_f32(sym[4 * g + 2], (b >> 16) | ((c & 0xFFu) << 16));
+      w[4 * g + 3] = merge_f32(sym[4 * g + 3], c >> 8);
     }
   }
 };
@@ -414,7 +424,7 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
 #pragma unroll
         for (int q = 0; q < S::IN_VECS; ++q) nxt[q] = ld_cg_v4(in + (size_t)un * 16 * ES + 16 * q);
       }
-      uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 1];
+      alignas(16) uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 16];
       S::split(v, sy, rw);
       *reinterpret_cast<uint4*>(&sm.syms[u * 16]) = *reinterpret_cast<const uint4*>(sy);
       if (RB > 0) {
@@ -710,7 +720,7 @@ LZ_DEV void merge_store(const char* __restrict__ raw, const DecSmem& sm, uint32_
   const uint32_t tid = threadIdx.x;
   const uint32_t units = n / 16;
   for (uint32_t u = tid; u < units; u += blockDim.x) {
-    uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 16];
+    alignas(16) uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 16];
 #pragma unroll
     for (int q = 0; q < S::RAW_BYTES / 16; ++q)
       reinterpret_cast<uint4*>(rw)[q] = ld_cg_v4(raw + (size_t)u * S::RAW_BYTES + 16 * q);
@@ -748,7 +758,7 @@ LZ_DEV void merge_accumulate(const char* __restrict__ raw, const DecSmem& sm, ui
   const uint32_t tid = threadIdx.x;
   const uint32_t units = (n + 15) / 16;
   for (uint32_t u = tid; u < units; u += blockDim.x) {
-    uint8_t rw[S::RAW_BYTES];
+    alignas(16) uint8_t rw[S::RAW_BYTES];
     uint8_t sy[16];
     if ((u + 1) * 16 <= n) {
 #pragma unroll

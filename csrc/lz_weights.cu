@@ -679,3 +679,71 @@ extern "C" int lz_emu_weight_broadcast_relay(LzEmu* e, int src, const void* cons
   LZ_CUDA_TRY(cudaStreamSynchronize(s));
   return LZE_OK;
 }
+
+// ----------------------------------------------------------------------------
+// Copy-engine point-to-point transfer into a receiver's symmetric tensors.
+// The bytes move by DMA (cudaMemcpyAsync into the peer's heap mapping), so no
+// SM is used for the data; two one-thread kernels carry the protocol:
+//   receiver: post "clear to send" (its earlier stream work on the
+//             destinations is done), then wait until the sender's "ready";
+//   sender:   wait for "clear to send", issue one copy per tensor on the same
+//             stream, then post "ready" (stream order puts it after the copies'
+//             completion, so the receiver's acquire sees the bytes).
+// Flags: per (sender, receiver) pair, value = sequence number of the pair.
+// ----------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kCeReady = 491520;        // [src] u64 in the receiver's heap
+constexpr size_t kCeCredit = 491520 + 64;  // [receiver] u64 in the sender's heap
+static_assert(kCeCredit + 64 <= (512u << 10), "copy-engine flags reach the test word");
+static_assert(kRelayReady + LZ_MAX_RANKS * kRelayReadyStride <= kCeReady, "copy-engine flags overlap relay flags");
+
+__global__ void ce_signal_kernel(unsigned long long* flag, unsigned long long v) {
+  st_release_sys(flag, v);
+}
+
+__global__ void ce_wait_kernel(LzDevComm c, const unsigned long long* flag, unsigned long long v, int peer) {
+  lz_wait_ge(c, flag, v, 14, peer);
+}
+
+}  // namespace
+
+// role 0: sender to `peer`; role 1: receiver from `peer`. Sender arrays (host
+// memory): source pointers, destination heap offsets and sizes of n tensors.
+extern "C" int lz_weight_transfer_ce(LzComm* c, int role, int peer, const unsigned long long* src_ptrs,
+                                     const unsigned long long* dst_offs, const unsigned long long* sizes,
+                                     unsigned int n, unsigned long long seq, cudaStream_t s) {
+  const int W = c->dev.world, me = c->dev.rank;
+  if (peer < 0 || peer >= W || peer == me) {
+    lz_set_error("copy-engine transfer: bad peer %d", peer);
+    return LZE_ARG;
+  }
+  if (role == 0) {
+    for (unsigned int i = 0; i < n; ++i) {
+      if (dst_offs[i] + sizes[i] > c->heap_bytes) {
+        lz_set_error("copy-engine transfer: destination %u outside the heap", i);
+        return LZE_ARG;
+      }
+    }
+    const unsigned long long* credit =
+        reinterpret_cast<const unsigned long long*>(c->dev.heap[me] + kCeCredit) + peer;
+    ce_wait_kernel<<<1, 1, 0, s>>>(c->dev, credit, seq, peer);
+    LZ_CUDA_TRY(cudaGetLastError());
+    for (unsigned int i = 0; i < n; ++i) {
+      if (!sizes[i]) continue;
+      LZ_CUDA_TRY(cudaMemcpyAsync(c->dev.heap[peer] + dst_offs[i], reinterpret_cast<const void*>(src_ptrs[i]),
+                                  sizes[i], cudaMemcpyDeviceToDevice, s));
+    }
+    unsigned long long* ready = reinterpret_cast<unsigned long long*>(c->dev.heap[peer] + kCeReady) + me;
+    ce_signal_kernel<<<1, 1, 0, s>>>(ready, seq);
+    LZ_CUDA_TRY(cudaGetLastError());
+  } else {
+    unsigned long long* credit = reinterpret_cast<unsigned long long*>(c->dev.heap[peer] + kCeCredit) + me;
+    ce_signal_kernel<<<1, 1, 0, s>>>(credit, seq);
+    LZ_CUDA_TRY(cudaGetLastError());
+    const unsigned long long* ready = reinterpret_cast<const unsigned long long*>(c->dev.heap[me] + kCeReady) + peer;
+    ce_wait_kernel<<<1, 1, 0, s>>>(c->dev, ready, seq, peer);
+    LZ_CUDA_TRY(cudaGetLastError());
+  }
+  return LZE_OK;
+}

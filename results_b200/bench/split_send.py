@@ -27,7 +27,9 @@ from ..utils import csvfmt
 
 def parse():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--modes", default="raw,split,nccl")
+    ap.add_argument("--modes", default="raw,split,nccl",
+                    help="raw, split (split+rANS), nccl, direct (zero copy into a symmetric receive buffer), "
+                         "ce (the same by copy-engine DMA)")
     ap.add_argument("--dtype", default="bfloat16")
     ap.add_argument("--min-bytes", type=int, default=256)
     ap.add_argument("--max-bytes", type=int, default=1 << 30)
@@ -54,7 +56,11 @@ def main():
     from results_b200.parallel import weights
     from results_b200.utils.sm_budget import SmBudget
 
-    comm = lz.init(config=Config(user_bytes=16 * MiB, stage_bytes=512 * MiB, timeout_s=60.0))
+    direct = bool({"direct", "ce"} & set(a.modes.split(",")))
+    if direct and world != 2:
+        raise SystemExit("modes 'direct' and 'ce' (zero copy into a symmetric receive buffer) run on exactly 2 ranks")
+    comm = lz.init(config=Config(user_bytes=(a.max_bytes + 64 * MiB) if direct else 16 * MiB,
+                                 stage_bytes=512 * MiB, timeout_s=60.0))
     dtype = getattr(torch, a.dtype)
     es = torch.empty((), dtype=dtype).element_size()
     budget = SmBudget(local, a.sm_budget) if a.sm_budget else None
@@ -76,6 +82,10 @@ def main():
             x = torch.empty_like(x)
         chunk = (a.chunk_mb * MiB // es) if a.chunk_mb else n
         parts = [x[i:i + chunk] for i in range(0, n, chunk)]
+        if direct:
+            comm.reset_alloc()
+            sym = comm.empty(n, dtype)
+            sym_parts = [sym[i:i + chunk] for i in range(0, n, chunk)]
         for mode in a.modes.split(","):
             def once():
                 if mode == "nccl":
@@ -84,6 +94,11 @@ def main():
                             dist.send(p, 1)
                         elif rank == 1:
                             dist.recv(p, 0)
+                elif mode == "direct":
+                    engines["raw"].broadcast_direct(sym_parts, 0, src_tensors=parts if rank == 0 else None,
+                                                    relay=False)
+                elif mode == "ce":
+                    engines["raw"].send_copy_engine(sym_parts, 0, 1, src_tensors=parts if rank == 0 else None)
                 else:
                     eng = engines[mode]
                     for p in parts:

@@ -8,7 +8,8 @@ Modes
   ours_split   native transfer, split+rANS encoded (bit-exact), same paths
   ours_p2p     native point-to-point transfer to each receiver in turn (split+rANS)
   ours_direct  native zero-copy raw broadcast into receivers' symmetric weight tensors
-               (one multimem.st per 16 bytes reaches every receiver's weights)
+               (relay broadcast with multimem.st forwarding for more than 2 ranks)
+  ours_ce      copy-engine DMA into each receiver's symmetric weights (no SM moves data)
   nccl_bcast   per-tensor torch.distributed.broadcast, the reference's update path
                (back_up/update_weight_from_distributed.py:422-449)
   nccl_send    per-tensor send from rank 0 to every receiver (batched isend/irecv)
@@ -77,7 +78,7 @@ def main():
     fn = shapes.MODELS[a.model]
     specs = fn(layers=a.layers) if a.layers else fn()
     total_bytes = shapes.total_params(specs) * 2
-    direct = "ours_direct" in a.modes
+    direct = bool({"ours_direct", "ours_ce"} & set(a.modes.split(",")))
     user = (total_bytes + 256 * MiB) if direct else 64 * MiB
     comm = lz.init(config=Config(user_bytes=user, stage_bytes=512 * MiB, timeout_s=60.0))
     sd = shapes.make_state_dict(specs, seed=1, empty=(rank != 0))
@@ -96,6 +97,11 @@ def main():
         if mode == "ours_direct":
             dst = [sym_of[id(t)] for t in ts]
             engines["ours_raw"].broadcast_direct(dst, 0, src_tensors=ts if rank == 0 else None)
+            return
+        if mode == "ours_ce":  # copy-engine DMA into each receiver's symmetric weights, one after another
+            dst = [sym_of[id(t)] for t in ts]
+            for d in range(1, world):
+                engines["ours_raw"].send_copy_engine(dst, 0, d, src_tensors=ts if rank == 0 else None)
             return
         if mode in ("ours_raw", "ours_split"):
             eng = engines[mode]
@@ -135,7 +141,7 @@ def main():
         if world == 1:
             break
         if rank != 0:
-            for t in (sym if mode == "ours_direct" else tensors):
+            for t in (sym if mode in ("ours_direct", "ours_ce") else tensors):
                 t.fill_(0)
         for _ in range(a.warmup):
             run(mode, tensors)
@@ -154,7 +160,7 @@ def main():
         comm.check()
         ok = True
         if rank != 0:
-            got = sym if mode == "ours_direct" else tensors
+            got = sym if mode in ("ours_direct", "ours_ce") else tensors
             ok = all(checksum(t) == s for t, s in zip(got, ref_sums))
         okt = torch.tensor([0 if ok else 1])
         dist.all_reduce(okt, group=ctrl)

@@ -47,6 +47,8 @@ _native_sigs.add_cuda({
                                   C.c_uint64, C.c_void_p),
     "lz_emu_weight_broadcast_relay": (C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_void_p), C.c_uint, C.c_int,
                                       C.c_uint64, C.c_void_p),
+    "lz_weight_transfer_ce": (C.c_int, C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_uint64),
+                              C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.c_uint, C.c_uint64, C.c_void_p),
 })
 
 TG = 32768
@@ -184,6 +186,38 @@ class WeightTransfer:
             rows.append([srcp, d.data_ptr() - comm._local_base, d.numel() * d.element_size(), 0])
         t = torch.tensor(rows, dtype=torch.int64).pin_memory()
         return t.to(f"cuda:{comm.device}", non_blocking=True), len(rows)
+
+    def send_copy_engine(self, dst_tensors, src: int, dst: int, src_tensors=None) -> None:
+        """Zero-copy point-to-point transfer by DMA: rank `src` copies its
+        ``src_tensors`` (default: its own ``dst_tensors``) into rank `dst`'s
+        symmetric ``dst_tensors`` with the copy engines (no SM does the data
+        movement). Both ranks call; other ranks do nothing."""
+        comm = self.comm
+        me = comm.rank
+        if me not in (src, dst) or src == dst:
+            return
+        key = (src, dst)
+        s = self.pair_seq.get(key, 0) + 1
+        self.pair_seq[key] = s
+        st = torch.cuda.current_stream(comm.device)
+        n = len(dst_tensors)
+        if me == src:
+            srcs = src_tensors if src_tensors is not None else dst_tensors
+            ptrs = (C.c_uint64 * n)(*[t.data_ptr() for t in srcs])
+            offs, sizes = [], []
+            for t_s, t_d in zip(srcs, dst_tensors):
+                if not comm.is_symmetric(t_d):
+                    raise ValueError("copy-engine transfer needs destination tensors allocated with comm.empty()")
+                nb = t_d.numel() * t_d.element_size()
+                if t_s.numel() * t_s.element_size() != nb:
+                    raise ValueError("source and destination sizes differ")
+                offs.append(t_d.data_ptr() - comm._local_base)
+                sizes.append(nb)
+            rc = comm._lib.lz_weight_transfer_ce(comm.handle, 0, dst, ptrs, (C.c_uint64 * n)(*offs),
+                                                 (C.c_uint64 * n)(*sizes), n, s, st.cuda_stream)
+        else:
+            rc = comm._lib.lz_weight_transfer_ce(comm.handle, 1, src, None, None, None, 0, s, st.cuda_stream)
+        _native.check(rc, "copy-engine transfer")
 
     def broadcast_direct(self, dst_tensors, src: int, src_tensors=None, nblocks: int = 0,
                          relay: bool | None = None) -> None:

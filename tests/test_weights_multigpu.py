@@ -79,6 +79,17 @@ def _worker(rank, world, cases, dump_dir):
     comm.check()
     results.append(("raw", "broadcast_weights_symmetric", 0.0,
                     all(torch.equal(sym_sd[k].view(torch.int16), ref[k].view(torch.int16)) for k in ref)))
+    # copy-engine DMA 0 -> 1 into symmetric tensors (twice: the pair sequence moves on)
+    ce = [comm.empty(t.shape, t.dtype) for t in ref.values()]
+    for t in ce:
+        t.fill_(-2)
+    for _ in range(2):
+        wt.send_copy_engine(ce, 0, 1, src_tensors=list(ref.values()) if rank == 0 else None)
+    torch.cuda.synchronize()
+    comm.check()
+    if rank == 1:
+        results.append(("raw", "copy_engine", 0.0,
+                        all(torch.equal(a.view(torch.int16), b.view(torch.int16)) for a, b in zip(ce, ref.values()))))
     # dump oracle: rank 0 dumps, the others compare what they received with it
     if rank == 0:
         weights.dump_tensors(list(ref.items()), dump_dir, 3, 0, group_name="test")
