@@ -11,7 +11,8 @@ here is GLM-4-9B's: 40 layers, 2 KV heads of dim 128, 40 KB per token).
 
 Modes: nccl (batched isend/irecv per tensor), ours_raw and ours_split (the
 native point-to-point transfer kernel, raw or split+rANS encoded),
-ours_direct (zero-copy stores into the receiver's symmetric KV buffers).
+ours_direct (zero-copy SM stores into the receiver's symmetric KV buffers),
+ours_ce (the same by copy-engine DMA).
 Latency: CUDA events per rank around one whole request, max over ranks.
 Data: N(0, 1) activations from a fixed seed; receivers are checked bit-exact.
 """
@@ -28,7 +29,7 @@ from ..utils import csvfmt
 
 TOKENS = (7680, 10240, 15360, 25600, 51200, 76800, 102400)
 HEADER = ["Input Token", "nccl kv cache transfer latency (ms)", "ours_raw latency (ms)",
-          "ours_split latency (ms)", "ours_direct latency (ms)", "kv_bytes", "bitexact"]
+          "ours_split latency (ms)", "ours_direct latency (ms)", "ours_ce latency (ms)", "kv_bytes", "bitexact"]
 
 
 def _max(v: float, group) -> float:
@@ -82,7 +83,9 @@ def main(argv=None):
                     for w in dist.batch_isend_irecv([op]):
                         w.wait()
             elif mode == "ours_direct":
-                raw.broadcast_direct(sym, 0, src_tensors=src if rank == 0 else None, relay=False)
+                raw.broadcast_direct(sym, 0, src_tensors=src if rank == 0 else None, relay=False, copy_engine=False)
+            elif mode == "ours_ce":
+                raw.send_copy_engine(sym, 0, 1, src_tensors=src if rank == 0 else None)
             else:
                 eng = raw if mode == "ours_raw" else split
                 if rank == 0:
@@ -91,9 +94,9 @@ def main(argv=None):
                     eng.recv(dst, 0)
 
         res, exact = {}, True
-        for mode in ("nccl", "ours_raw", "ours_split", "ours_direct"):
+        for mode in ("nccl", "ours_raw", "ours_split", "ours_direct", "ours_ce"):
             if rank == 1:
-                for t in (sym if mode == "ours_direct" else dst):
+                for t in (sym if mode in ("ours_direct", "ours_ce") else dst):
                     t.fill_(0)
             for _ in range(a.warmup):
                 run(mode)
@@ -108,7 +111,7 @@ def main(argv=None):
             comm.check()
             res[mode] = _max(e0.elapsed_time(e1) / a.iters, ctrl)
             if rank == 1:
-                got = sym if mode == "ours_direct" else dst
+                got = sym if mode in ("ours_direct", "ours_ce") else dst
                 exact = exact and all(torch.equal(x.view(torch.int16), y.view(torch.int16))
                                       for x, y in zip(got, src))
         ok = torch.tensor([0 if exact else 1])
@@ -117,6 +120,7 @@ def main(argv=None):
                "ours_raw latency (ms)": round(res["ours_raw"], 3),
                "ours_split latency (ms)": round(res["ours_split"], 3),
                "ours_direct latency (ms)": round(res["ours_direct"], 3),
+               "ours_ce latency (ms)": round(res["ours_ce"], 3),
                "kv_bytes": T * per_tok, "bitexact": int(ok.item()) == 0}
         rows.append(row)
         if rank == 0:

@@ -96,7 +96,7 @@ def main():
                             dist.recv(p, 0)
                 elif mode == "direct":
                     engines["raw"].broadcast_direct(sym_parts, 0, src_tensors=parts if rank == 0 else None,
-                                                    relay=False)
+                                                    relay=False, copy_engine=False)
                 elif mode == "ce":
                     engines["raw"].send_copy_engine(sym_parts, 0, 1, src_tensors=parts if rank == 0 else None)
                 else:

@@ -220,18 +220,20 @@ class WeightTransfer:
         _native.check(rc, "copy-engine transfer")
 
     def broadcast_direct(self, dst_tensors, src: int, src_tensors=None, nblocks: int = 0,
-                         relay: bool | None = None) -> None:
+                         relay: bool | None = None, copy_engine: bool | None = None) -> None:
         """Zero-copy raw broadcast into symmetric destination tensors.
 
         Every rank passes its symmetric destination tensors (allocated with
         ``comm.empty`` in the same order on all ranks); the sender also passes
         ``src_tensors`` (default: its own destination tensors).
 
-        With more than two ranks (``relay`` default) the bytes are relayed:
-        the sender hands each 256 KB chunk to one owner rank, which forwards
-        it to every other rank (multimem.st through the switch when multicast
-        is available), so all GPUs' NVLink egress carries the broadcast and
-        every receiver takes in each byte once. Otherwise the sender stores
+        Two ranks (``copy_engine`` default): the copy engines move the bytes
+        (765 GB/s for 1 GB on 2 x B200, vs 643 GB/s for SM peer stores).
+        More than two ranks (``relay`` default): the sender hands each 256 KB
+        chunk to one owner rank, which forwards it to every other rank
+        (multimem.st through the switch when multicast is available), so all
+        GPUs' NVLink egress carries the broadcast and every receiver takes in
+        each byte once. ``relay=False, copy_engine=False``: the sender stores
         every chunk into every receiver itself.
         """
         comm = self.comm
@@ -239,6 +241,27 @@ class WeightTransfer:
             if src_tensors is not None:
                 for d, s_ in zip(dst_tensors, src_tensors):
                     d.copy_(s_)
+            return
+        if copy_engine is None:
+            copy_engine = comm.world == 2 and not relay
+        if copy_engine:
+            if comm.world != 2:
+                raise ValueError("the copy-engine path is point to point (2 ranks); use relay for more")
+            own = comm.rank == src and src_tensors is not None and any(
+                d_.data_ptr() != s_.data_ptr() for d_, s_ in zip(dst_tensors, src_tensors))
+            if own:
+                # the sender's own destination copy (the kernel paths write it too),
+                # on a side stream so it overlaps the DMA to the receiver
+                cur = torch.cuda.current_stream(comm.device)
+                side = self.__dict__.setdefault("_side", torch.cuda.Stream(comm.device))
+                side.wait_stream(cur)
+            self.send_copy_engine(dst_tensors, src, 1 - src, src_tensors=src_tensors)
+            if own:
+                with torch.cuda.stream(side):
+                    for d_, s_ in zip(dst_tensors, src_tensors):
+                        if d_.data_ptr() != s_.data_ptr():
+                            d_.copy_(s_)
+                cur.wait_stream(side)
             return
         me = comm.rank
         mask = ((1 << comm.world) - 1) & ~(1 << src)

@@ -53,8 +53,9 @@ def _worker(rank, world, cases, dump_dir):
     for t in sym:
         t.fill_(-3)
     wt = weights.WeightTransfer(comm, mode="raw")
-    for _ in range(2):
-        wt.broadcast_direct(sym, 0, src_tensors=list(ref.values()) if rank == 0 else None, nblocks=32)
+    for kernel_path in (False, True):  # the default (copy engines / relay), then the sender-store kernel
+        kw = {"relay": False, "copy_engine": False} if kernel_path else {}
+        wt.broadcast_direct(sym, 0, src_tensors=list(ref.values()) if rank == 0 else None, nblocks=32, **kw)
     torch.cuda.synchronize()
     comm.check()
     bad_idx = [i for i, (a, b) in enumerate(zip(sym, ref.values()))
