@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Headline benchmark: bf16 sum-allreduce bus bandwidth, 1 GiB per rank.
 
-The metric BASELINE.json names ("allreduce bus GB/s vs size @2/4/8 GPU") at
+The headline metric ("allreduce bus GB/s vs size @2/4/8 GPU") at
 the reference's headline message size (1 GB, csv/single_node_allreduce.csv:7
 and csv/allreduce_throughput.csv:8 of the reference). One rank per GPU.
 

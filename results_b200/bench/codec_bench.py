@@ -41,7 +41,7 @@ def make_data(n, dtype, dist="normal", std=0.02, seed=0):
     g = torch.Generator(device="cuda").manual_seed(seed)
     if dist == "normal":
         x = torch.randn(n, device="cuda", generator=g) * std
-    elif dist == "activation":  # N(0,1) with 1% outliers x50
+    elif dist == "activation":  # N(0,1) with 1% outliers x50 (activation-like)
         x = torch.randn(n, device="cuda", generator=g)
         m = torch.rand(n, device="cuda", generator=g) < 0.01
         x = torch.where(m, x * 50, x)

@@ -2,7 +2,7 @@
 results are quoted on (csv/weight_update_rl_GLM4_9B.csv and
 csv/weight_update_rl_qwen3.5_35B_A3B.csv of the reference).
 
-Weights are random N(0, 0.02) in bf16, norms 1.0 (BASELINE configs 4 and 5);
+Weights are random N(0, 0.02) in bf16, norms 1.0 (the weight-update benchmark configurations);
 tensor names follow the Hugging Face checkpoints so manifests and per-tensor
 CSV rows line up with the reference's (e.g. ``mlp.gate_up_proj`` = 214 MB).
 """
@@ -60,7 +60,7 @@ def qwen35_a3b_specs(layers: int = 40, hidden: int = 2048, heads: int = 16, kv_h
 
     Routed experts are coalesced per layer into two stacked tensors
     (gate_up [E, 2*ffn, hidden] and down [E, hidden, ffn]), i.e. chunks far
-    above 64 MB, as BASELINE config 5 asks.
+    above 64 MB, as the MoE weight-update configuration specifies.
     """
     q, kv = heads * head_dim, kv_heads * head_dim
     out = [TensorSpec("model.embed_tokens.weight", (vocab, hidden))]

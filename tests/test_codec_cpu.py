@@ -1,5 +1,5 @@
 """CPU oracle of the LZC1 codec: lossless round trips, format validation and
-measured compression ratios (bf16 split round trip with a
+measured compression ratios (the CPU configuration: bf16 split round trip with a
 reference CPU rANS of the exponent stream on 16M N(0, 0.02) elements)."""
 import pytest
 import torch
@@ -50,7 +50,7 @@ def test_uint8_and_fp8_roundtrip():
 
 
 def test_ratio_bf16_16M_normal():
-    """16M-element N(0, 0.02) bf16 tensor."""
+    """16M-element N(0, 0.02) bf16 tensor, reference CPU rANS of the exponent stream."""
     n = 16 * 1024 * 1024
     x = _rand(n, torch.bfloat16, std=0.02, seed=0)
     blob = codec.encode_cpu(x)

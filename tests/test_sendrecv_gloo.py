@@ -1,5 +1,5 @@
 """Send/recv reference algorithms on gloo CPU ranks, checked against
-torch.distributed.all_reduce (fp32 and bf16 at 1 KB, 1 MB
+torch.distributed.all_reduce (the CPU/gloo configuration: fp32 and bf16 at 1 KB, 1 MB
 and 64 MB, values N(0,1) from torch.manual_seed(0))."""
 import pytest
 import torch
@@ -58,7 +58,7 @@ def test_algorithms_small(world):
 
 
 def test_algorithms_64mb_world2():
-    """BASELINE config 1 at the 64 MB size: ring, two-shot and RHD."""
+    """The CPU/gloo configuration at the 64 MB size: ring, two-shot and RHD."""
     res = run_ranks(_worker, 2, backend="gloo",
                     args=(["ring_sendrecv", "naive_twoshot", "rhd_sendrecv", "twoshot_collective"],
                           ["64MB"], ["float32", "bfloat16"], None), timeout=600)
