@@ -40,6 +40,7 @@ struct DecSmem {
   uint32_t ent[256];      // table entries (sym << 16 | freq)
   TgHeader h;
   int ok;
+  alignas(8) uint64_t bar;  // mbarrier of the bulk copy that stages `sec`
 };
 
 LZ_DEV uint32_t lane_id() { return threadIdx.x & 31; }
@@ -615,20 +616,39 @@ LZ_DEV bool decode_tg_syms(const char* __restrict__ src, uint32_t cap, uint32_t 
   } else {
     const uint32_t nnz = sm.h.nnz, nsub = sm.h.nsub;
     // stage the whole ANS section (<= pad16(n) bytes) so every word fetch of
-    // the rANS loop is a shared-memory load, off the global-latency path
+    // the rANS loop is a shared-memory load, off the global-latency path: one
+    // bulk copy by the TMA engine (vector loads if it is not 16-byte aligned)
     {
-      const uint32_t sb = sm.h.sym_bytes, step = blockDim.x * 16;
-      uint32_t o = tid * 16;
-      for (; o + 3 * step < sb; o += 4 * step) {
-        uint4 v[4];
+      const uint32_t sb = sm.h.sym_bytes;
+      const bool bulk = ((reinterpret_cast<uintptr_t>(symsec) | smem_addr(sm.sec) | sb) & 15u) == 0 && sb > 0;
+      if (bulk) {
+        if (tid == 0) mbar_init(&sm.bar, 1);
+        fence_proxy_async_smem();  // earlier generic writes to this shared memory come first
+        __syncthreads();
+        if (tid == 0) {
+          fence_mbar_init();
+          bulk_g2s(sm.sec, symsec, sb, &sm.bar);
+        }
+        // a global -> shared bulk copy always completes; the bound only keeps
+        // a broken environment from spinning forever
+        if (!mbar_wait(&sm.bar, 0, 1u << 26) && tid == 0) sm.ok = 0;
+        __syncthreads();
+        if (tid == 0) mbar_inval(&sm.bar);
+      } else {
+        const uint32_t step = blockDim.x * 16;
+        uint32_t o = tid * 16;
+        for (; o + 3 * step < sb; o += 4 * step) {
+          uint4 v[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = ld_cg_v4(symsec + o + u * step);
+          for (int u = 0; u < 4; ++u) v[u] = ld_cg_v4(symsec + o + u * step);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(&sm.sec[o + u * step]) = v[u];
+          for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(&sm.sec[o + u * step]) = v[u];
+        }
+        for (; o < sb; o += step) *reinterpret_cast<uint4*>(&sm.sec[o]) = ld_cg_v4(symsec + o);
       }
-      for (; o < sb; o += step) *reinterpret_cast<uint4*>(&sm.sec[o]) = ld_cg_v4(symsec + o);
     }
     __syncthreads();
+    if (!sm.ok) return false;
     symsec = reinterpret_cast<const char*>(sm.sec);
     // decode table: slot -> entry, by binary search over the cumulative table
     uint32_t* s_cum = sm.cum;

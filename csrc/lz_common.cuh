@@ -54,6 +54,55 @@ LZ_DEV int ld_volatile_i32(const int* p) {
 LZ_DEV void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 LZ_DEV void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
+// ----------------------------------------------------------------------------
+// Bulk asynchronous copy global -> this CTA's shared memory (the TMA engine,
+// no multicast) completing on an mbarrier. Addresses and size must be
+// multiples of 16 bytes; callers check and fall back to vector loads.
+// ----------------------------------------------------------------------------
+LZ_DEV uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+LZ_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+LZ_DEV void mbar_inval(uint64_t* bar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// Generic-proxy shared-memory writes made so far are ordered before later
+// async-proxy (bulk copy) accesses of the same memory.
+LZ_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+LZ_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+// One thread: announce `bytes` of transaction on `bar` and start the copy.
+LZ_DEV void bulk_g2s(void* dst_smem, const void* src_global, uint32_t bytes, uint64_t* bar) {
+  uint64_t state;
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 %0, [%1], %2;"
+               : "=l"(state)
+               : "r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+  (void)state;
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst_smem)),
+      "l"(src_global), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Bounded wait for phase `parity` of `bar`; false after max_iters polls.
+LZ_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t max_iters) {
+  for (uint32_t it = 0; it < max_iters; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
 // 16-byte global loads/stores. `cg` bypasses L1 for data another GPU wrote.
 // These are compiler intrinsics, not volatile asm, so loads of later loop
 // iterations can be scheduled early; ordering against flag waits is kept
