@@ -86,3 +86,51 @@ def test_trace_ranges_and_bucket_logs(caplog):
     with caplog.at_level(logging.INFO, logger="results_b200"):
         weights._log_bucket("send", 3, [("a", torch.zeros(1024)), ("b", torch.zeros(256, dtype=torch.bfloat16))])
     assert any("[BUCKET] send 3 start tensors=2" in r.getMessage() for r in caplog.records)
+
+
+def test_size_table_choices():
+    """The measured size table: ll for small messages, one-shot, then two-shot
+    or NVLS by world; unaligned sizes never get a vector-only algorithm."""
+    from results_b200.parallel.tuning import choose
+
+    KB, MB = 1 << 10, 1 << 20
+    assert choose(1 * KB, 2, True, True) == "ll"
+    assert choose(256 * KB, 2, True, True) == "ll"
+    assert choose(4 * MB, 2, True, True) == "oneshot"
+    assert choose(1 << 30, 2, True, True) == "twoshot"
+    assert choose(128 * KB, 8, True, True) == "ll"
+    assert choose(512 * KB, 8, True, True) == "oneshot"
+    assert choose(4 * MB, 8, True, True) == "twoshot"
+    assert choose(64 * MB, 8, True, True) == "nvls"
+    assert choose(64 * MB, 8, False, True) == "twoshot"
+    assert choose(1 << 30, 4, True, True) == "nvls"
+    assert choose(64 * MB, 4, True, True) == "twoshot"
+    assert choose(1000 * 2 + 2, 8, True, True) == "oneshot"  # not a multiple of 16 bytes
+
+
+def test_bench_baseline_ratio_uses_aggregates():
+    import importlib.util
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(root, "bench.py"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    assert abs(m.REF_AGGREGATE_1GB[8] - 53.60 * 8) < 1e-9
+    assert abs(m.REF_AGGREGATE_1GB[2] - 54.68 * 2) < 1e-9
+    assert 1 not in m.REF_AGGREGATE_1GB and 4 not in m.REF_AGGREGATE_1GB
+
+
+def test_config_env_and_bounds_library_name(monkeypatch):
+    from results_b200.config import Config
+    from results_b200.utils import build
+
+    monkeypatch.setenv("LZ_RATIO_BUDGET", "0.7")
+    assert Config.from_env().ratio_budget == 0.7
+    monkeypatch.setenv("LZ_BOUNDS", "1")
+    assert build.cuda_lib_name() == "liblz_cuda_bounds.so"
+    monkeypatch.setenv("LZ_BOUNDS", "0")
+    assert build.cuda_lib_name() == "liblz_cuda.so"
+    # the heap holds flags, one-shot buffers, low-latency areas, stage and user region
+    c = Config(user_bytes=64 << 20, stage_bytes=32 << 20, oneshot_bytes=4 << 20)
+    assert c.total_heap_bytes() >= (1 << 20) + 2 * (4 << 20) + (8 << 20) + (32 << 20) + (64 << 20)
