@@ -8,12 +8,17 @@ multi-node form. Counterpart of single_node_nccl_allreduce_benchmark/run.sh:21-4
 (``run.sh local`` -> 2 local GPUs, otherwise a 2-node torchrun). Every
 launch is bounded by ``timeout -k 60`` well above the process-group
 timeout so ranks that wait on each other end with an error.
+
+``--gdbserver PORT`` starts rank 0 under ``gdbserver :PORT`` (the other ranks
+run normally), the counterpart of back_up/mpi_gdbserver.sh:1-48: attach a
+debugger to the first rank while the job runs.
 """
 from __future__ import annotations
 
 import argparse
 import os
 import shlex
+import shutil
 import socket
 import subprocess
 import sys
@@ -27,15 +32,23 @@ def _free_port() -> int:
     return p
 
 
+# rank 0 under gdbserver, the others as usual ("$@" = python arguments)
+_GDB_WRAPPER = ('if [ "$RANK" = "0" ]; then exec gdbserver ":$LZ_GDB_PORT" "$LZ_PYTHON" "$@"; '
+                'else exec "$LZ_PYTHON" "$@"; fi')
+
+
 def build_command(mode: str, nproc: int, rest: list[str], nnodes: int = 1, node_rank: int = 0,
                   master_addr: str = "127.0.0.1", master_port: int | None = None,
-                  timeout_s: int = 3600) -> list[str]:
+                  timeout_s: int = 3600, gdbserver_port: int | None = None) -> list[str]:
     port = master_port or _free_port()
     cmd = ["timeout", "-k", "60", str(timeout_s), sys.executable, "-m", "torch.distributed.run",
            f"--nnodes={nnodes if mode == 'node' else 1}", f"--nproc-per-node={nproc}",
            f"--master-addr={master_addr if mode == 'node' else '127.0.0.1'}", f"--master-port={port}"]
     if mode == "node":
         cmd.append(f"--node-rank={node_rank}")
+    if gdbserver_port:
+        # torchrun then runs `bash -c WRAPPER lz-rank <python args>` in every rank
+        cmd += ["--no-python", "bash", "-c", _GDB_WRAPPER, "lz-rank"]
     return cmd + rest
 
 
@@ -49,13 +62,22 @@ def main(argv=None):
     ap.add_argument("--master-port", type=int, default=None)
     ap.add_argument("--timeout", type=int, default=3600)
     ap.add_argument("--dry-run", action="store_true")
+    ap.add_argument("--gdbserver", type=int, default=None, metavar="PORT",
+                    help="run rank 0 under gdbserver listening on PORT")
     a, rest = ap.parse_known_args(argv)
-    cmd = build_command(a.mode, a.nproc, rest, a.nnodes, a.node_rank, a.master_addr, a.master_port, a.timeout)
+    cmd = build_command(a.mode, a.nproc, rest, a.nnodes, a.node_rank, a.master_addr, a.master_port, a.timeout,
+                        gdbserver_port=a.gdbserver)
+    env = dict(os.environ)
+    env.setdefault("NCCL_DEBUG", "WARN")
+    if a.gdbserver:
+        env["LZ_GDB_PORT"] = str(a.gdbserver)
+        env["LZ_PYTHON"] = sys.executable
     if a.dry_run:
         print(shlex.join(cmd))
         return 0
-    env = dict(os.environ)
-    env.setdefault("NCCL_DEBUG", "WARN")
+    if a.gdbserver and not shutil.which("gdbserver"):
+        print("gdbserver is not installed on this machine", file=sys.stderr)
+        return 2
     return subprocess.call(cmd, env=env)
 
 

@@ -134,3 +134,26 @@ def test_config_env_and_bounds_library_name(monkeypatch):
     # the heap holds flags, one-shot buffers, low-latency areas, stage and user region
     c = Config(user_bytes=64 << 20, stage_bytes=32 << 20, oneshot_bytes=4 << 20)
     assert c.total_heap_bytes() >= (1 << 20) + 2 * (4 << 20) + (8 << 20) + (32 << 20) + (64 << 20)
+
+
+def test_launch_gdbserver_wraps_rank0_only(tmp_path):
+    """--gdbserver runs rank 0 under gdbserver and the others plainly: the
+    wrapper is checked by running it with a fake gdbserver on PATH."""
+    import os
+    import subprocess
+    import sys
+
+    from results_b200 import launch
+
+    cmd = launch.build_command("local", 2, ["-c", "print(1)"], gdbserver_port=1234)
+    i = cmd.index("--no-python")
+    assert cmd[i + 1:i + 5] == ["bash", "-c", launch._GDB_WRAPPER, "lz-rank"]
+    fake = tmp_path / "gdbserver"
+    fake.write_text("#!/bin/sh\necho gdbserver \"$@\"\n")
+    fake.chmod(0o755)
+    base = dict(os.environ, PATH=f"{tmp_path}:{os.environ['PATH']}", LZ_GDB_PORT="1234", LZ_PYTHON=sys.executable)
+    out0 = subprocess.run(["bash", "-c", launch._GDB_WRAPPER, "lz-rank", "-c", "print('rank')"],
+                          env=dict(base, RANK="0"), capture_output=True, text=True).stdout
+    out1 = subprocess.run(["bash", "-c", launch._GDB_WRAPPER, "lz-rank", "-c", "print('rank')"],
+                          env=dict(base, RANK="1"), capture_output=True, text=True).stdout
+    assert out0.startswith("gdbserver :1234 ") and out1.strip() == "rank"
