@@ -5,7 +5,8 @@ The reference renders its figures with matplotlib/seaborn
 available in this image, so the same figures (bandwidth vs size per
 variant, grouped bars per configuration) are written as standalone SVG.
 
-    python -m results_b200.utils.plots sweep out.csv fig.svg   # schema-A allreduce sweep
+    python -m results_b200.utils.plots sweep out.csv fig.svg   # schema-A allreduce sweep (bus GB/s)
+    python -m results_b200.utils.plots latency out.csv fig.svg # the same, time per call (log)
     python -m results_b200.utils.plots codec codec.csv fig.svg # schema-D codec table
 """
 from __future__ import annotations
@@ -23,8 +24,8 @@ def _esc(s) -> str:
 
 
 def line_chart(series: dict, path: str, title: str = "", xlabel: str = "", ylabel: str = "",
-               logx: bool = True, width: int = 760, height: int = 440) -> str:
-    """series: {label: [(x, y), ...]} -> SVG file."""
+               logx: bool = True, width: int = 760, height: int = 440, logy: bool = False) -> str:
+    """series: {label: [(x, y), ...]} -> SVG file (log2 x axis; optional log10 y axis)."""
     pts = [p for s in series.values() for p in s if p[1] is not None]
     if not pts:
         raise ValueError("no data")
@@ -35,16 +36,21 @@ def line_chart(series: dict, path: str, title: str = "", xlabel: str = "", ylabe
     L, R, T, B = 70, 170, 40, 60
     W, H = width - L - R, height - T - B
     X = lambda v: L + (fx(v) - x0) / ((x1 - x0) or 1) * W
-    Y = lambda v: T + H - v / y1 * H
+    if logy:
+        ly0 = math.floor(math.log10(max(min(p[1] for p in pts), 1e-12)))
+        ly1 = math.ceil(math.log10(y1))
+        Y = lambda v: T + H - (math.log10(max(v, 1e-12)) - ly0) / ((ly1 - ly0) or 1) * H
+    else:
+        Y = lambda v: T + H - v / y1 * H
     out = [f'<svg xmlns="http://www.w3.org/2000/svg" width="{width}" height="{height}" font-family="sans-serif" font-size="12">',
            f'<rect width="{width}" height="{height}" fill="white"/>',
            f'<text x="{width / 2}" y="22" text-anchor="middle" font-size="15">{_esc(title)}</text>',
            f'<line x1="{L}" y1="{T + H}" x2="{L + W}" y2="{T + H}" stroke="black"/>',
            f'<line x1="{L}" y1="{T}" x2="{L}" y2="{T + H}" stroke="black"/>']
-    for k in range(6):
-        v = y1 * k / 5
+    ticks = [10.0 ** e for e in range(ly0, ly1 + 1)] if logy else [y1 * k / 5 for k in range(6)]
+    for v in ticks:
         out.append(f'<line x1="{L}" y1="{Y(v):.1f}" x2="{L + W}" y2="{Y(v):.1f}" stroke="#ddd"/>')
-        out.append(f'<text x="{L - 6}" y="{Y(v) + 4:.1f}" text-anchor="end">{v:.0f}</text>')
+        out.append(f'<text x="{L - 6}" y="{Y(v) + 4:.1f}" text-anchor="end">{v:g}</text>')
     xticks = sorted({p[0] for p in pts})
     step = max(1, len(xticks) // 8)
     for xv in xticks[::step]:
@@ -93,6 +99,20 @@ def sweep_chart(csv_path: str, svg_path: str, metric: str = "cuda_ms", bus: bool
                       xlabel="message size", ylabel="GB/s")
 
 
+def sweep_latency_chart(csv_path: str, svg_path: str, metric: str = "cuda_ms") -> str:
+    """Per-call time (us, log scale) vs message size for every variant."""
+    series: dict = {}
+    ws = ""
+    with open(csv_path) as f:
+        for r in csv.DictReader(f):
+            if r.get("metric") != metric:
+                continue
+            ws = r.get("world_size", ws)
+            series.setdefault(r["variant"], []).append((int(r["size_bytes"]), float(r["variant_ms"]) * 1e3))
+    return line_chart(series, svg_path, title=f"allreduce time per call, {ws} x B200",
+                      xlabel="message size", ylabel="us (log)", logy=True)
+
+
 def codec_chart(csv_path: str, svg_path: str) -> str:
     comp, dec = [], []
     with open(csv_path) as f:
@@ -105,5 +125,5 @@ def codec_chart(csv_path: str, svg_path: str) -> str:
 
 if __name__ == "__main__":
     kind, src, dst = sys.argv[1:4]
-    (sweep_chart if kind == "sweep" else codec_chart)(src, dst)
+    {"sweep": sweep_chart, "latency": sweep_latency_chart, "codec": codec_chart}[kind](src, dst)
     print(dst)
