@@ -26,6 +26,7 @@ import ctypes as C
 import json
 import os
 import time
+import weakref
 
 import torch
 import torch.distributed as dist
@@ -324,15 +325,19 @@ def buckets(named, max_bytes: int):
         yield cur
 
 
+_ENGINES: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+
+
 def _engine(comm, mode, **kw):
+    """One engine per (communicator, mode, options); dropped with the communicator."""
     from .allreduce import get_comm, init
 
     comm = comm or get_comm() or init()
-    key = (id(comm), mode, tuple(sorted(kw.items())))
-    cache = _engine.__dict__.setdefault("cache", {})
-    if key not in cache:
-        cache[key] = WeightTransfer(comm, mode=mode, **kw)
-    return cache[key]
+    per_comm = _ENGINES.setdefault(comm, {})
+    key = (mode, tuple(sorted(kw.items())))
+    if key not in per_comm:
+        per_comm[key] = WeightTransfer(comm, mode=mode, **kw)
+    return per_comm[key]
 
 
 def _progress(items, what: str):

@@ -50,3 +50,30 @@ def test_dump_manifest_roundtrip(tmp_path):
     assert rec["num_tensors"] == 2 and rec["tensors"][0]["shape"] == [8, 4]
     back = weights.load_dump(str(tmp_path), 12)
     assert torch.equal(back["a.weight"].view(torch.int16), named[0][1].view(torch.int16))
+
+
+def test_engine_cache_is_per_communicator_object():
+    """Engines are cached per communicator object (not per id(), which a new
+    communicator can reuse) and released with it."""
+    import gc
+
+    from results_b200.parallel import weights
+
+    class FakeComm:
+        rank, world, device, sm_count = 0, 1, 0, 148
+
+    made = []
+    orig = weights.WeightTransfer
+    weights.WeightTransfer = lambda comm, mode, **kw: made.append(mode) or object()
+    try:
+        a = FakeComm()
+        e1 = weights._engine(a, "raw")
+        assert weights._engine(a, "raw") is e1
+        assert weights._engine(a, "split_ans") is not e1
+        del a
+        gc.collect()
+        b = FakeComm()
+        weights._engine(b, "raw")
+        assert len(made) == 3 and len(weights._ENGINES) == 1
+    finally:
+        weights.WeightTransfer = orig
