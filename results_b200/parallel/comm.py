@@ -252,6 +252,11 @@ class Communicator:
         if self._closed:
             return
         self._closed = True
+        import sys
+
+        w = sys.modules.get("results_b200.parallel.weights")
+        if w is not None:  # cached weight engines hold this communicator
+            w._ENGINES.pop(self, None)
         try:
             torch.cuda.synchronize(self.device)
         except Exception:
@@ -267,6 +272,11 @@ class Communicator:
         if self._closed:
             return
         self._closed = True
+        import sys
+
+        w = sys.modules.get("results_b200.parallel.weights")
+        if w is not None:  # cached weight engines hold this communicator
+            w._ENGINES.pop(self, None)
         try:
             torch.cuda.synchronize(self.device)
             self.barrier_host()
