@@ -7,6 +7,8 @@ variant, grouped bars per configuration) are written as standalone SVG.
 
     python -m results_b200.utils.plots sweep out.csv fig.svg   # schema-A allreduce sweep (bus GB/s)
     python -m results_b200.utils.plots latency out.csv fig.svg # the same, time per call (log)
+    python -m results_b200.utils.plots kv kv.csv fig.svg       # KV-cache transfer latency vs tokens
+    python -m results_b200.utils.plots weights fig.svg a.json b.json  # weight-update bars
     python -m results_b200.utils.plots codec codec.csv fig.svg # schema-D codec table
 """
 from __future__ import annotations
@@ -113,6 +115,77 @@ def sweep_latency_chart(csv_path: str, svg_path: str, metric: str = "cuda_ms") -
                       xlabel="message size", ylabel="us (log)", logy=True)
 
 
+def bar_chart(groups: dict, path: str, title: str = "", ylabel: str = "", width: int = 760,
+              height: int = 440) -> str:
+    """groups: {group label: {series label: value}} -> grouped-bar SVG."""
+    labels = []
+    for g in groups.values():
+        for k in g:
+            if k not in labels:
+                labels.append(k)
+    vmax = max((v for g in groups.values() for v in g.values() if v is not None), default=1.0) * 1.1 or 1.0
+    L, R, T, B = 70, 170, 40, 70
+    W, H = width - L - R, height - T - B
+    gw = W / max(1, len(groups))
+    bw = gw * 0.8 / max(1, len(labels))
+    out = [f'<svg xmlns="http://www.w3.org/2000/svg" width="{width}" height="{height}" font-family="sans-serif" font-size="12">',
+           f'<rect width="{width}" height="{height}" fill="white"/>',
+           f'<text x="{width / 2}" y="22" text-anchor="middle" font-size="15">{_esc(title)}</text>',
+           f'<line x1="{L}" y1="{T + H}" x2="{L + W}" y2="{T + H}" stroke="black"/>',
+           f'<line x1="{L}" y1="{T}" x2="{L}" y2="{T + H}" stroke="black"/>']
+    for k in range(6):
+        v = vmax * k / 5
+        y = T + H - v / vmax * H
+        out.append(f'<line x1="{L}" y1="{y:.1f}" x2="{L + W}" y2="{y:.1f}" stroke="#ddd"/>')
+        out.append(f'<text x="{L - 6}" y="{y + 4:.1f}" text-anchor="end">{v:.3g}</text>')
+    for gi, (gl, g) in enumerate(groups.items()):
+        x0 = L + gi * gw + gw * 0.1
+        for si, sl in enumerate(labels):
+            v = g.get(sl)
+            if v is None:
+                continue
+            h = v / vmax * H
+            out.append(f'<rect x="{x0 + si * bw:.1f}" y="{T + H - h:.1f}" width="{bw * 0.9:.1f}" height="{h:.1f}" '
+                       f'fill="{PALETTE[si % len(PALETTE)]}"/>')
+        out.append(f'<text x="{L + gi * gw + gw / 2:.1f}" y="{T + H + 18}" text-anchor="middle">{_esc(gl)}</text>')
+    out.append(f'<text x="18" y="{T + H / 2}" text-anchor="middle" transform="rotate(-90 18 {T + H / 2})">{_esc(ylabel)}</text>')
+    for si, sl in enumerate(labels):
+        ly = T + 14 + 18 * si
+        out.append(f'<rect x="{L + W + 15}" y="{ly - 9}" width="12" height="12" fill="{PALETTE[si % len(PALETTE)]}"/>')
+        out.append(f'<text x="{L + W + 32}" y="{ly + 1}">{_esc(sl)}</text>')
+    out.append("</svg>")
+    with open(path, "w") as f:
+        f.write("\n".join(out))
+    return path
+
+
+def weight_update_chart(json_paths: list, svg_path: str) -> str:
+    """Seconds per update by mode, one group per weight_update JSON (model x world)."""
+    import json as _json
+
+    groups = {}
+    for jp in json_paths:
+        with open(jp) as f:
+            d = _json.load(f)
+        groups[f"{d.get('model')} x{d.get('world')}"] = {m: r["sec"] for m, r in d["results"].items()}
+    return bar_chart(groups, svg_path, title="RL weight update, seconds per update (lower is better)",
+                     ylabel="s")
+
+
+def kv_chart(csv_path: str, svg_path: str) -> str:
+    """KV-cache transfer latency (ms) vs input tokens for every mode column."""
+    series: dict = {}
+    with open(csv_path) as f:
+        for r in csv.DictReader(f):
+            tok = int(r["Input Token"])
+            for k, v in r.items():
+                if k.endswith("(ms)") and v not in ("", None):
+                    series.setdefault(k.replace(" latency (ms)", "").replace(" kv cache transfer", ""), []).append(
+                        (tok, float(v)))
+    return line_chart(series, svg_path, title="prefill -> decode KV-cache transfer, 2 x B200",
+                      xlabel="input tokens", ylabel="ms")
+
+
 def codec_chart(csv_path: str, svg_path: str) -> str:
     comp, dec = [], []
     with open(csv_path) as f:
@@ -125,5 +198,9 @@ def codec_chart(csv_path: str, svg_path: str) -> str:
 
 if __name__ == "__main__":
     kind, src, dst = sys.argv[1:4]
-    {"sweep": sweep_chart, "latency": sweep_latency_chart, "codec": codec_chart}[kind](src, dst)
+    if kind == "weights":  # plots weights out.svg a.json b.json ...
+        weight_update_chart(sys.argv[3:], src)
+        print(src)
+        sys.exit(0)
+    {"sweep": sweep_chart, "latency": sweep_latency_chart, "codec": codec_chart, "kv": kv_chart}[kind](src, dst)
     print(dst)

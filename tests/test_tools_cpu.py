@@ -157,3 +157,25 @@ def test_launch_gdbserver_wraps_rank0_only(tmp_path):
     out1 = subprocess.run(["bash", "-c", launch._GDB_WRAPPER, "lz-rank", "-c", "print('rank')"],
                           env=dict(base, RANK="1"), capture_output=True, text=True).stdout
     assert out0.startswith("gdbserver :1234 ") and out1.strip() == "rank"
+
+
+def test_result_charts(tmp_path):
+    """Grouped bars, KV latency and log-scale latency charts render valid SVG."""
+    import json
+
+    from results_b200.utils import csvfmt, plots
+
+    kv = tmp_path / "kv.csv"
+    kv.write_text("Input Token,nccl kv cache transfer latency (ms),ours_ce latency (ms)\n"
+                  "7680,2.7,0.8\n102400,8.3,6.0\n")
+    assert plots.kv_chart(str(kv), str(tmp_path / "kv.svg")).endswith("kv.svg")
+    wj = tmp_path / "w.json"
+    wj.write_text(json.dumps({"model": "glm4-9b", "world": 2, "results": {"a": {"sec": 0.03}, "b": {"sec": 0.02}}}))
+    svg = open(plots.weight_update_chart([str(wj)], str(tmp_path / "w.svg"))).read()
+    assert svg.startswith("<svg") and svg.count("<rect") >= 3
+    rows = [{"metric": "cuda_ms", "size_label": "1 KB", "size_bytes": 1024, "world_size": 2, "variant": v,
+             "variant_ms": ms} for v, ms in (("NCCL", 0.0145), ("LL", 0.0043))]
+    rows += [{**r, "size_bytes": 2048, "size_label": "2 KB"} for r in rows]
+    sweep = tmp_path / "a.csv"
+    csvfmt.write_rows(str(sweep), csvfmt.SCHEMA_A, rows)
+    assert "us (log)" in open(plots.sweep_latency_chart(str(sweep), str(tmp_path / "l.svg"))).read()
