@@ -45,9 +45,12 @@ def stage_bytes_needed(numel: int, dtype: torch.dtype, world: int, compress: boo
 def all_to_all(x: torch.Tensor, out: torch.Tensor | None = None, compress: bool = False, comm=None,
                nblocks: int = 0, stream=None) -> torch.Tensor:
     """Exchange equal chunks: chunk j of every rank's ``x`` lands as chunk
-    ``rank`` of rank j's output. CPU tensors go through ``dist.all_to_all_single``."""
+    ``rank`` of rank j's output. CPU tensors go through ``dist.all_to_all_single``
+    (``compress=True``: LZC1 streams of the CPU codec, sizes exchanged first)."""
     if not x.is_cuda:
         res = torch.empty_like(x) if out is None else out
+        if compress:
+            return _all_to_all_compressed_cpu(x.contiguous(), res)
         dist.all_to_all_single(res, x.contiguous())
         return res
     from .allreduce import get_comm, init
@@ -72,3 +75,35 @@ def all_to_all(x: torch.Tensor, out: torch.Tensor | None = None, compress: bool 
                                  nblocks, s.cuda_stream)
     _native.check(rc, "all_to_all")
     return out
+
+
+def _all_to_all_compressed_cpu(x: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
+    """Host-side compressed all-to-all over any backend: every chunk is
+    encoded with the CPU codec, the stream sizes are exchanged, then the
+    streams (padded to the largest) and each received stream is decoded into
+    its place. Lossless: the result equals the raw all-to-all bit for bit."""
+    from ..ops import codec
+
+    world = dist.get_world_size(group)
+    if x.numel() % world:
+        raise ValueError(f"{x.numel()} elements do not split into {world} equal chunks")
+    if x.dtype not in COMPRESSIBLE:
+        raise ValueError(f"compressed all_to_all supports {COMPRESSIBLE}, got {x.dtype}")
+    chunks = x.view(world, -1)
+    blobs = [codec.encode_cpu(chunks[j]) for j in range(world)]
+    sizes = torch.tensor([b.numel() for b in blobs], dtype=torch.int64)
+    got_sizes = torch.empty_like(sizes)
+    dist.all_to_all_single(got_sizes, sizes, group=group)
+    cap_t = sizes.max().reshape(1)
+    dist.all_reduce(cap_t, op=dist.ReduceOp.MAX, group=group)  # one padded size on every rank
+    cap = int(cap_t.item())
+    send = torch.zeros(world, cap, dtype=torch.uint8)
+    for j, b in enumerate(blobs):
+        send[j, : b.numel()] = b
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    o = out.view(world, -1)
+    for j in range(world):
+        o[j].copy_(codec.decode_cpu(recv[j, : int(got_sizes[j])], o.shape[1], x.dtype))
+    return out
+
