@@ -325,6 +325,63 @@ def buckets(named, max_bytes: int):
         yield cur
 
 
+# ------------------------------------------------------------ host transport
+class HostTransfer:
+    """Weight transfer of CPU tensors over any torch.distributed backend
+    (gloo): per tensor, raw bytes, or an LZC1 stream of the CPU codec with its
+    size sent first (``split_ans``). The same public calls (send / recv /
+    broadcast) as :class:`WeightTransfer`; receivers end bit-identical."""
+
+    def __init__(self, mode: str = "split_ans", group=None):
+        if mode not in MODES:
+            raise ValueError(f"mode must be one of {MODES}")
+        self.mode, self.group = mode, group
+
+    def _encode(self, t):
+        return codec.encode_cpu(t) if self.mode == "split_ans" and t.dtype in _CODEC_DTYPES else None
+
+    def send(self, tensors, dsts) -> None:
+        dsts = [dsts] if isinstance(dsts, int) else list(dsts)
+        for t in tensors:
+            blob = self._encode(t)
+            for d in dsts:
+                if blob is None:
+                    dist.send(t.contiguous(), d, group=self.group)
+                else:
+                    dist.send(torch.tensor([blob.numel()], dtype=torch.int64), d, group=self.group)
+                    dist.send(blob, d, group=self.group)
+
+    def recv(self, tensors, src: int) -> None:
+        for t in tensors:
+            if self.mode != "split_ans" or t.dtype not in _CODEC_DTYPES:
+                buf = t if t.is_contiguous() else torch.empty_like(t)
+                dist.recv(buf, src, group=self.group)
+                if buf is not t:
+                    t.copy_(buf)
+                continue
+            n = torch.empty(1, dtype=torch.int64)
+            dist.recv(n, src, group=self.group)
+            blob = torch.empty(int(n.item()), dtype=torch.uint8)
+            dist.recv(blob, src, group=self.group)
+            t.copy_(codec.decode_cpu(blob, t.numel(), t.dtype).view(t.shape))
+
+    def broadcast(self, tensors, src: int) -> None:
+        me, world = dist.get_rank(self.group), dist.get_world_size(self.group)
+        if me == src:
+            self.send(tensors, [r for r in range(world) if r != src])
+        else:
+            self.recv(tensors, src)
+
+
+_CODEC_DTYPES = (torch.bfloat16, torch.float16, torch.float32) + tuple(
+    d for d in (getattr(torch, "float8_e4m3fn", None), getattr(torch, "float8_e5m2", None)) if d is not None)
+
+
+def _host(state_dict) -> bool:
+    ts = list(state_dict.values()) if isinstance(state_dict, dict) else list(state_dict)
+    return bool(ts) and all(not t.is_cuda for t in ts)
+
+
 _ENGINES: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
 
 
@@ -358,14 +415,18 @@ def _log_bucket(what: str, i: int, bucket) -> None:
 
 def send_weights(state_dict, dst, comm=None, mode: str = "split_ans", bucket_bytes: int | None = None,
                  dump_dir: str | None = None, weight_version: int = 0, **kw) -> None:
-    """Send a state_dict (name -> CUDA tensor) to rank(s) `dst`, bucket by bucket."""
-    eng = _engine(comm, mode, **kw)
+    """Send a state_dict (name -> tensor) to rank(s) `dst`, bucket by bucket
+    (CUDA tensors: native kernels; CPU tensors: :class:`HostTransfer`)."""
+    eng = HostTransfer(mode) if _host(state_dict) else _engine(comm, mode, **kw)
+    if isinstance(eng, HostTransfer):
+        bucket_bytes = bucket_bytes or (512 << 20)
     bb = bucket_bytes or eng.comm.config.update_weight_buffer_bytes
+    me = dist.get_rank() if isinstance(eng, HostTransfer) else eng.comm.rank
     trace.log.info("[START] send_weights version=%d mode=%s dst=%s", weight_version, mode, dst)
     for i, bucket in enumerate(_progress(list(buckets(list(state_dict.items()), bb)), "send_weights")):
         _log_bucket("send", i, bucket)
         if dump_dir:
-            dump_tensors(bucket, dump_dir, weight_version, i, group_name=f"src{eng.comm.rank}")
+            dump_tensors(bucket, dump_dir, weight_version, i, group_name=f"src{me}")
         with trace.range(f"send_weights.bucket{i}"):
             eng.send([t for _, t in bucket], dst)
 
@@ -373,8 +434,8 @@ def send_weights(state_dict, dst, comm=None, mode: str = "split_ans", bucket_byt
 def recv_weights(state_dict, src: int, comm=None, mode: str = "split_ans", bucket_bytes: int | None = None,
                  **kw) -> dict:
     """Receive into the destination tensors of `state_dict` (same names, shapes, order)."""
-    eng = _engine(comm, mode, **kw)
-    bb = bucket_bytes or eng.comm.config.update_weight_buffer_bytes
+    eng = HostTransfer(mode) if _host(state_dict) else _engine(comm, mode, **kw)
+    bb = bucket_bytes or (512 << 20 if isinstance(eng, HostTransfer) else eng.comm.config.update_weight_buffer_bytes)
     for i, bucket in enumerate(_progress(list(buckets(list(state_dict.items()), bb)), "recv_weights")):
         _log_bucket("recv", i, bucket)
         with trace.range(f"recv_weights.bucket{i}"):
@@ -391,6 +452,11 @@ def broadcast_weights(state_dict, src: int = 0, comm=None, mode: str = "split_an
     through :meth:`WeightTransfer.broadcast_direct` (relay broadcast for more
     than two ranks): no slots and no receiver copies, in one launch.
     """
+    if _host(state_dict):
+        eng = HostTransfer(mode)
+        for bucket in buckets(list(state_dict.items()), bucket_bytes or (512 << 20)):
+            eng.broadcast([t for _, t in bucket], src)
+        return state_dict
     eng = _engine(comm, mode, **kw)
     tensors = list(state_dict.values())
     if mode == "raw" and tensors and all(t.is_cuda and eng.comm.is_symmetric(t) for t in tensors):
