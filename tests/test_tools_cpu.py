@@ -179,3 +179,23 @@ def test_result_charts(tmp_path):
     sweep = tmp_path / "a.csv"
     csvfmt.write_rows(str(sweep), csvfmt.SCHEMA_A, rows)
     assert "us (log)" in open(plots.sweep_latency_chart(str(sweep), str(tmp_path / "l.svg"))).read()
+
+
+def test_low_latency_flag_values():
+    """The low-latency one-shot's call flags (odd-multiplier hash of the call
+    number, low bit set; the same formula as ll_flag in csrc/lz_allreduce.cu)
+    are never 0 (zeroed memory) and never repeat within 2^31 uses of one
+    parity area, so a stale word can never carry the current flag."""
+    import numpy as np
+
+    e = np.arange(0, 1 << 22, dtype=np.uint64)
+    f = (((e + 1) * np.uint64(0x9E3779B1)) & np.uint64(0xFFFFFFFF)) | np.uint64(1)
+    assert (f != 0).all()
+    for parity in (0, 1):
+        v = f[parity::2]
+        assert np.unique(v).size == v.size
+    import re
+
+    src = open(__import__("os").path.join(__import__("os").path.dirname(__file__), "..", "csrc",
+                                          "lz_allreduce.cu")).read()
+    assert re.search(r"\(uint32_t\)\(epoch \+ 1ull\) \* 0x9E3779B1u\) \| 1u", src)
