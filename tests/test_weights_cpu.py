@@ -77,3 +77,68 @@ def test_engine_cache_is_per_communicator_object():
         assert len(made) == 3 and len(weights._ENGINES) == 1
     finally:
         weights.WeightTransfer = orig
+
+
+def _fake_comm(world, rank=0, symmetric=True):
+    import torch
+
+    from results_b200.parallel import weights
+
+    calls = []
+
+    class Lib:
+        def __getattr__(self, name):
+            def f(*args):
+                calls.append(name)
+                return 0
+            return f
+
+    class Comm:
+        pass
+
+    c = Comm()
+    c.world, c.rank, c.device, c.sm_count = world, rank, 0, 148
+    c._lib = Lib()
+    c.handle = None
+    c._local_base = 0
+    c.has_multicast = True
+    c.is_symmetric = lambda t: symmetric
+    wt = weights.WeightTransfer.__new__(weights.WeightTransfer)
+    wt.comm, wt.pair_seq, wt.bcast_seq = c, {}, {}
+    return wt, calls, torch
+
+
+def test_zero_copy_dispatch_policy(monkeypatch):
+    """broadcast_direct picks copy engines for 2 ranks with large tensors, the
+    peer-store kernel for 2 ranks with small ones, and the relay for more."""
+    import torch
+
+    from results_b200.parallel import weights
+
+    seen = []
+    monkeypatch.setattr(weights.WeightTransfer, "send_copy_engine",
+                        lambda self, d, src, dst, src_tensors=None: seen.append(("ce", src, dst)))
+    monkeypatch.setattr(weights.WeightTransfer, "_direct_descs",
+                        lambda self, d, s: (torch.zeros(1, dtype=torch.int64), len(d)))
+    monkeypatch.setattr(weights, "_native", type("N", (), {"check": staticmethod(lambda rc, what: None)}))
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: type("S", (), {"cuda_stream": 0})())
+
+    big = [torch.empty(0)] * 2
+    monkeypatch.setattr(torch.Tensor, "numel", lambda self: 32 << 20, raising=False)
+    wt, calls, _ = _fake_comm(2, rank=1)
+    wt.broadcast_direct(big, 0)
+    assert seen == [("ce", 0, 1)] and not calls
+
+    monkeypatch.setattr(torch.Tensor, "numel", lambda self: 1 << 10, raising=False)
+    seen.clear()
+    wt, calls, _ = _fake_comm(2, rank=1)
+    wt.broadcast_direct(big, 0)
+    assert not seen and calls == ["lz_weight_transfer_direct"]
+
+    wt, calls, _ = _fake_comm(8, rank=3)
+    wt.broadcast_direct(big, 0)
+    assert calls == ["lz_weight_broadcast_relay"]
+
+    wt, calls, _ = _fake_comm(8, rank=3)
+    wt.broadcast_direct(big, 0, relay=False, copy_engine=False)
+    assert calls == ["lz_weight_transfer_direct"]
