@@ -3,9 +3,14 @@
 // (compressed allreduce, weight transfer), which write/read records directly
 // in peer or multicast memory.
 //
-// One CTA of LZC_THREADS = 4 warps handles one TG (4 sub-blocks of 8192
+// One CTA of LZC_THREADS = 8 warps handles one TG (8 sub-blocks of 4096
 // symbols, one warp per sub-block). Output is bit-identical to the CPU oracle
 // (csrc/cpu/lz_cpu.cpp).
+//
+// Reference behaviour being re-designed: the dietgpu float codec the
+// reference calls as a closed library (exponent byte ANS-coded with local
+// tables, sign/mantissa raw; ratios and GB/s in raw/dietgpu_walltime_*.csv,
+// local vs global tables in plot/local_frequency_compression_ratio.py:9-19).
 #pragma once
 #include "lz_codec_format.h"
 #include "lz_common.cuh"

@@ -5,6 +5,12 @@ with ``python -m results_b200.bench.allreduce_sweep``; the table is keyed by
 world size. Until a world size has been measured the defaults below apply:
 one-shot for latency-bound messages, NVLS (switch reduction) for large ones
 when a multicast object exists, else two-shot.
+
+The reference picks by size too, with fixed thresholds: halving-doubling up
+to HD_MAX_MB and K-channel rings by size
+(16_node_nccl_allreduce_benchmark/ring_sendrecv_allreduce.py:33-36,254-313),
+and a fused all-source reduce below 1 M elements
+(single_node_nccl_allreduce_benchmark/compressed_p2p_kernel.cu:304-305).
 """
 from __future__ import annotations
 
