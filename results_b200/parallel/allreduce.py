@@ -57,6 +57,20 @@ def select_algo(nbytes: int, world: int, has_multicast: bool, symmetric: bool,
     return choose(nbytes, world, has_multicast, symmetric)
 
 
+def _padded_allreduce(comm, t: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+    """Large tensor whose size or address is not a multiple of 16 bytes: the
+    vector kernels run on a zero-padded aligned copy (zeros add nothing to the
+    sum), and the result is copied back."""
+    es = t.element_size()
+    pad = (-(t.numel() * es) % 16) // es
+    tmp = torch.zeros(t.numel() + pad, dtype=t.dtype, device=t.device)
+    tmp[: t.numel()].copy_(t.reshape(-1))
+    comm.allreduce_(tmp, algo="twoshot")
+    res = t if out is None else out
+    res.copy_(tmp[: t.numel()].view(t.shape))
+    return res
+
+
 @traced("allreduce")
 def allreduce(t: torch.Tensor, algo: str = "auto", out: torch.Tensor | None = None,
               comm: Communicator | None = None, group=None) -> torch.Tensor:
@@ -77,13 +91,12 @@ def allreduce(t: torch.Tensor, algo: str = "auto", out: torch.Tensor | None = No
         algo = select_algo(t.numel() * t.element_size(), comm.world, comm.has_multicast,
                            comm.is_symmetric(t) and (out is None or comm.is_symmetric(out)),
                            comm.config)
-        if algo != "oneshot" and (t.data_ptr() % 16 or (out is not None and out.data_ptr() % 16)):
-            if t.numel() * t.element_size() <= comm.config.oneshot_bytes:
+        nbytes = t.numel() * t.element_size()
+        if algo != "oneshot" and (nbytes % 16 or t.data_ptr() % 16 or (out is not None and out.data_ptr() % 16)):
+            if nbytes <= comm.config.oneshot_bytes:
                 algo = "oneshot"
-            else:  # vector kernels need 16-byte aligned buffers: go through an aligned copy
-                tmp = t.contiguous().clone()
-                comm.allreduce_(tmp, algo="twoshot" if tmp.numel() * tmp.element_size() % 16 == 0 else "oneshot")
-                return (t if out is None else out).copy_(tmp)
+            else:
+                return _padded_allreduce(comm, t, out)
     if algo not in NATIVE:
         raise ValueError(f"unknown allreduce algorithm {algo!r}")
     return comm.allreduce_(t, out, algo=algo)
