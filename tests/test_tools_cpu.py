@@ -199,3 +199,38 @@ def test_low_latency_flag_values():
     src = open(__import__("os").path.join(__import__("os").path.dirname(__file__), "..", "csrc",
                                           "lz_allreduce.cu")).read()
     assert re.search(r"\(uint32_t\)\(epoch \+ 1ull\) \* 0x9E3779B1u\) \| 1u", src)
+
+
+def test_clock_sampler_with_fake_nvml(monkeypatch):
+    """Clock sampling reads NVML only (a fake module here): median SM clock of
+    the busy samples, the union of event reasons, idle samples ignored."""
+    import sys
+    import time
+    import types
+
+    from results_b200.utils import clocks
+
+    state = {"i": 0}
+    seq = [(1965, 0x0), (1800, 0x4), (1900, 0x4), (300, 0x1)]  # busy, power cap, power cap, idle
+
+    def clock(h, which):
+        return seq[state["i"] % len(seq)][0]
+
+    def reasons(h):
+        r = seq[state["i"] % len(seq)][1]
+        state["i"] += 1
+        return r
+
+    fake = types.SimpleNamespace(
+        NVML_CLOCK_SM=0, nvmlInit=lambda: None, nvmlDeviceGetHandleByIndex=lambda d: d,
+        nvmlDeviceGetMaxClockInfo=lambda h, w: 1965, nvmlDeviceGetClockInfo=clock,
+        nvmlDeviceGetPowerUsage=lambda h: 700_000, nvmlDeviceGetCurrentClocksEventReasons=reasons)
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    s = clocks.ClockSampler([0], period_s=0.001).start()
+    while state["i"] < 8:
+        time.sleep(0.001)
+    summ = s.stop().summary()
+    assert summ["sm_max_mhz"] == 1965 and summ["samples"] >= 8
+    assert summ["reasons"] == ["sw_power_cap"]
+    assert 1800 <= summ["sm_mhz"] <= 1965
+    assert clocks.decode_reasons(0x8 | 0x40) == ["hw_slowdown", "hw_thermal_slowdown"]
