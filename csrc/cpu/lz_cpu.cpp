@@ -6,9 +6,12 @@
 // the reference, loaded at single_node_nccl_allreduce_benchmark/compressed_twoshot_allreduce.py:34-47)
 // and the fp8 pair packer of back_up/fp8_e4m3fn_pack_benchmark.cu:21-93.
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
+#include <thread>
 #include <vector>
 
 #include "../lz_codec_format.h"
@@ -293,7 +296,46 @@ int lzc_tg_decode(const void* rec_, uint64_t rec_cap, void* out, uint32_t n, int
   return 0;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Worker threads for the whole-tensor calls: environment LZ_CPU_THREADS, else
+// the hardware concurrency (at most 32), never more than there are TGs.
+unsigned cpu_threads(uint64_t ntg) {
+  const char* e = getenv("LZ_CPU_THREADS");
+  unsigned t = e ? (unsigned)atoi(e) : std::thread::hardware_concurrency();
+  if (t < 1) t = 1;
+  if (t > 32) t = 32;
+  if ((uint64_t)t > ntg) t = (unsigned)(ntg ? ntg : 1);
+  return t;
+}
+
+// Runs fn(t) for t in [0, ntg) on cpu_threads(ntg) threads (dynamic split).
+template <class F>
+void parallel_tgs(uint64_t ntg, F fn) {
+  const unsigned nt = cpu_threads(ntg);
+  if (nt <= 1) {
+    for (uint64_t t = 0; t < ntg; ++t) fn(t);
+    return;
+  }
+  std::atomic<uint64_t> next{0};
+  std::vector<std::thread> pool;
+  pool.reserve(nt);
+  for (unsigned k = 0; k < nt; ++k)
+    pool.emplace_back([&]() {
+      for (uint64_t t = next++; t < ntg; t = next++) fn(t);
+    });
+  for (auto& th : pool) th.join();
+}
+
+}  // namespace
+
+extern "C" {
+
 // Whole-tensor compact stream. Returns bytes written or a negative code.
+// Table groups are encoded in parallel into per-TG scratch, then packed in
+// order, so the stream is the same byte for byte whatever the thread count.
 int64_t lzc_encode(const void* data, uint64_t n, int dt, void* out_, uint64_t cap) {
   if (cap < max_stream_bytes(n, dt)) return -1;
   uint8_t* out = static_cast<uint8_t*>(out_);
@@ -309,13 +351,21 @@ int64_t lzc_encode(const void* data, uint64_t n, int dt, void* out_, uint64_t ca
   uint64_t off = sizeof(StreamHeader) + pad16_64(8 * ntg);
   memset(out + sizeof(StreamHeader), 0, pad16_64(8 * ntg));
   const int es = elem_bytes(dt);
-  for (uint64_t t = 0; t < ntg; ++t) {
+  const uint64_t tcap = tg_capacity(dt);
+  std::vector<uint8_t> scratch(ntg * tcap);
+  std::vector<int64_t> sizes(ntg, 0);
+  parallel_tgs(ntg, [&](uint64_t t) {
     const uint32_t tn = (uint32_t)std::min<uint64_t>(TG_ELEMS, n - t * TG_ELEMS);
+    sizes[t] = lzc_tg_encode(static_cast<const uint8_t*>(data) + t * TG_ELEMS * es, tn, dt, &scratch[t * tcap]);
+  });
+  std::vector<uint64_t> offs(ntg);
+  for (uint64_t t = 0; t < ntg; ++t) {
+    if (sizes[t] < 0) return sizes[t];
+    offs[t] = off;
     memcpy(out + sizeof(StreamHeader) + 8 * t, &off, 8);
-    int64_t sz = lzc_tg_encode(static_cast<const uint8_t*>(data) + t * TG_ELEMS * es, tn, dt, out + off);
-    if (sz < 0) return sz;
-    off += (uint64_t)sz;
+    off += (uint64_t)sizes[t];
   }
+  parallel_tgs(ntg, [&](uint64_t t) { memcpy(out + offs[t], &scratch[t * tcap], (size_t)sizes[t]); });
   sh.total_bytes = off;
   memcpy(out, &sh, sizeof(sh));
   return (int64_t)off;
@@ -330,15 +380,21 @@ int lzc_decode(const void* stream_, uint64_t bytes, void* out, uint64_t n, int d
       sh.tg_elems != TG_ELEMS || sh.n_tg != num_tgs(n) || sh.total_bytes > bytes)
     return -3;
   const int es = elem_bytes(dt);
-  for (uint64_t t = 0; t < sh.n_tg; ++t) {
+  std::atomic<int> first_err{0};
+  parallel_tgs(sh.n_tg, [&](uint64_t t) {
     uint64_t off;
     memcpy(&off, st + sizeof(StreamHeader) + 8 * t, 8);
-    if (off >= sh.total_bytes) return -4;
-    const uint32_t tn = (uint32_t)std::min<uint64_t>(TG_ELEMS, n - t * TG_ELEMS);
-    int rc = lzc_tg_decode(st + off, sh.total_bytes - off, static_cast<uint8_t*>(out) + t * TG_ELEMS * es, tn, dt);
-    if (rc) return rc;
-  }
-  return 0;
+    int rc = -4;
+    if (off < sh.total_bytes) {
+      const uint32_t tn = (uint32_t)std::min<uint64_t>(TG_ELEMS, n - t * TG_ELEMS);
+      rc = lzc_tg_decode(st + off, sh.total_bytes - off, static_cast<uint8_t*>(out) + t * TG_ELEMS * es, tn, dt);
+    }
+    if (rc) {
+      int expect = 0;
+      first_err.compare_exchange_strong(expect, rc);
+    }
+  });
+  return first_err.load();
 }
 
 // Symbol histogram (for entropy reporting).

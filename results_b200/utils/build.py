@@ -41,7 +41,7 @@ NVCC_FLAGS = ARCH + [
     "-diag-suppress=177",
 ]
 CXX = os.environ.get("CXX", "g++")
-CPU_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-shared", "-Wall", "-march=x86-64-v2"]
+CPU_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-shared", "-Wall", "-march=x86-64-v2", "-pthread"]
 
 CUDA_LIB = LIB_DIR / "liblz_cuda.so"
 CPU_LIB = LIB_DIR / "liblz_cpu.so"

@@ -115,3 +115,26 @@ def test_decode_from_fixed_size_padded_buffer():
     msg[: blob.numel()] = blob
     y = codec.decode_cpu(msg, x.numel(), x.dtype)
     assert torch.equal(y.view(torch.int16), x.view(torch.int16))
+
+
+def test_cpu_stream_identical_for_any_thread_count():
+    """The CPU oracle encodes table groups on several threads and packs them in
+    order: the stream bytes do not depend on LZ_CPU_THREADS (a subprocess per
+    setting, since the variable is read by the native library)."""
+    import os
+    import subprocess
+    import sys
+
+    code = ("import torch,hashlib\nfrom results_b200.ops import codec\n"
+            "g=torch.Generator().manual_seed(3)\nx=(torch.randn(1_000_003,generator=g)*0.02).to(torch.bfloat16)\n"
+            "b=codec.encode_cpu(x)\ny=codec.decode_cpu(b,x.numel(),x.dtype)\n"
+            "assert torch.equal(x.view(torch.int16),y.view(torch.int16))\n"
+            "print(hashlib.sha256(b.numpy().tobytes()).hexdigest())\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    outs = set()
+    for n in ("1", "3", "16"):
+        env = dict(os.environ, LZ_CPU_THREADS=n, PYTHONPATH=root)
+        r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, cwd=root)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.add(r.stdout.strip())
+    assert len(outs) == 1
