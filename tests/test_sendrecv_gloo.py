@@ -120,3 +120,34 @@ def test_isend_irecv_fill_pattern_consistency(world):
     rank, which counts wrong bytes; repeated rounds change the pattern."""
     res = run_ranks(_pattern_worker, world, args=(3 << 20, 3))
     assert res == [0] * world, res
+
+
+def _odd_worker(rank, world, n):
+    import torch
+    import torch.distributed as dist
+
+    from results_b200.parallel import sendrecv
+
+    torch.manual_seed(0)
+    xs = [torch.randn(n) for _ in range(world)]
+    exact = torch.stack(xs).sum(0)
+    out = []
+    for algo in ("naive_twoshot", "ring_sendrecv", "twoshot_collective", "multichannel_ring"):
+        t = xs[rank].clone()
+        sendrecv.allreduce(t, algo)
+        out.append((algo, float((t - exact).abs().max())))
+    if world & (world - 1) == 0:
+        t = xs[rank].clone()
+        sendrecv.allreduce(t, "rhd_sendrecv")
+        out.append(("rhd_sendrecv", float((t - exact).abs().max())))
+    return out
+
+
+@pytest.mark.parametrize("world,n", [(3, 1001), (4, 7), (2, 1)])
+def test_algorithms_uneven_sizes(world, n):
+    """Element counts that do not divide by the world size (and smaller than
+    it): every send/recv algorithm still sums exactly (fp32, tolerance of the
+    summation order)."""
+    res = run_ranks(_odd_worker, world, backend="gloo", args=(n,), timeout=300)
+    bad = [r for rr in res for r in rr if not r[1] <= 1e-5]
+    assert not bad, bad
