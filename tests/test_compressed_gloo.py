@@ -60,3 +60,12 @@ def test_incompressible_ring():
     res = run_ranks(_worker, 4, backend="gloo", args=("compressed_ring", 50_000, "float32", 0.65, "uniform"),
                     timeout=300)
     assert all(r[0] for r in res), res
+
+
+@pytest.mark.parametrize("variant,world,n", [("compressed_twoshot", 3, 10_001), ("compressed_ring", 3, 10_001),
+                                             ("compressed_twoshot", 4, 3)])
+def test_variants_uneven_sizes(variant, world, n):
+    """Element counts that do not divide by the world size, down to fewer
+    elements than ranks: chunks of unequal (or zero) length still reduce."""
+    res = run_ranks(_worker, world, backend="gloo", args=(variant, n, "float32", 0.9, "normal"), timeout=300)
+    assert all(r[0] for r in res), res
