@@ -138,3 +138,22 @@ def test_cpu_stream_identical_for_any_thread_count():
         assert r.returncode == 0, r.stderr[-2000:]
         outs.add(r.stdout.strip())
     assert len(outs) == 1
+
+
+@pytest.mark.parametrize("n", [0, 1, 15, 16, 17, 32767, 32768, 32769])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32, torch.uint8])
+def test_roundtrip_edge_lengths(n, dtype):
+    """Empty tensors, tails shorter than a 16-element unit and table-group
+    boundaries round-trip bit-exactly."""
+    x = _rand(n, dtype) if dtype != torch.uint8 else torch.randint(0, 256, (n,), dtype=torch.uint8)
+    y = codec.decode_cpu(codec.encode_cpu(x), n, dtype)
+    assert torch.equal(x.view(torch.uint8), y.view(torch.uint8))
+
+
+@pytest.mark.parametrize("n", [0, 1, 2, 3, 1001])
+@pytest.mark.parametrize("dtype", [torch.float8_e4m3fn, torch.float8_e5m2])
+def test_fp8_odd_lengths(n, dtype):
+    """fp8 tensors with an odd element count (a half-filled last pair container)."""
+    x = (torch.randn(n, generator=torch.Generator().manual_seed(n)) * 0.5).to(dtype)
+    y = codec.decode_cpu(codec.encode_cpu(x), n, dtype)
+    assert torch.equal(x.view(torch.uint8), y.view(torch.uint8))
