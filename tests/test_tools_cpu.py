@@ -234,3 +234,24 @@ def test_clock_sampler_with_fake_nvml(monkeypatch):
     assert summ["reasons"] == ["sw_power_cap"]
     assert 1800 <= summ["sm_mhz"] <= 1965
     assert clocks.decode_reasons(0x8 | 0x40) == ["hw_slowdown", "hw_thermal_slowdown"]
+
+
+def test_report_regenerates_quoted_tables():
+    """The summary tables are regenerated from the committed measurements, and
+    the headline claim (auto >= NCCL at every size and rank count) holds in
+    the data."""
+    import os
+
+    from results_b200.utils import report
+
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "results")
+    text = report.main([root])
+    assert "| 1 GB |" in text and "Weight update" in text
+    import glob
+    import re
+
+    for p in glob.glob(os.path.join(root, "csv", "allreduce_sweep_*xB200_graph.csv")):
+        d = report.sweep_times(p)
+        for size, r in d.items():
+            assert r["Auto"] <= r["NCCL"] * 1.0001, (p, size, r["Auto"], r["NCCL"])
+    assert re.search(r"Smallest margin over NCCL: 1\.\d\dx", text)
