@@ -101,3 +101,41 @@ def wait_for_peers(hb: Heartbeat, timeout_s: float = 10.0) -> None:
             if time.time() > deadline:
                 raise
             time.sleep(0.05)
+
+
+_GENERATION = [0]
+
+
+def rebuild_world(lost, timeout_s: float = 60.0, backend: str | None = None) -> tuple[int, int]:
+    """Elastic shrink: the surviving ranks re-form the default process group
+    without the `lost` ranks and return their (new rank, new world size).
+
+    Every survivor calls it (between steps, with nothing in flight) after a
+    :class:`PeerLost`. The default group is torn down locally, then
+    re-initialised over the same rendezvous store under a per-generation
+    prefix, so stale keys of the old group never mix with the new one. Ranks
+    keep their order. The store must outlive the lost ranks (torchrun's agent
+    store does; with a rank-hosted store, rank 0 must survive). Native
+    communicators of the old group are abandoned by the caller
+    (``Communicator.abandon``) and created anew on the new group.
+    """
+    store = _store()
+    old_rank, old_world = dist.get_rank(), dist.get_world_size()
+    backend = backend or dist.get_backend()
+    survivors = [r for r in range(old_world) if r not in set(lost)]
+    if old_rank not in survivors:
+        raise ValueError(f"rank {old_rank} is listed as lost")
+    _GENERATION[0] += 1
+    gen = _GENERATION[0]
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass
+    import datetime
+
+    new_rank, new_world = survivors.index(old_rank), len(survivors)
+    prefix = dist.PrefixStore(f"lz/gen{gen}/", store)
+    dist.init_process_group(backend=backend, store=prefix, rank=new_rank, world_size=new_world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+    return new_rank, new_world
+
