@@ -20,6 +20,15 @@ __version__ = "0.1.0"
 from .config import Config  # noqa: F401
 
 
+__all__ = ["Config", "Communicator", "init", "allreduce", "get_comm", "shutdown", "select_algo",
+           "compressed_allreduce", "all_to_all", "send_weights", "recv_weights", "broadcast_weights",
+           "WeightTransfer", "encode", "decode", "pack_fp8", "unpack_fp8"]
+
+
+def __dir__():
+    return sorted(set(globals()) | set(__all__))
+
+
 def __getattr__(name):
     # Lazy imports keep `import results_b200` cheap and CPU-safe.
     if name in ("init", "allreduce", "get_comm", "shutdown", "select_algo"):

@@ -255,3 +255,12 @@ def test_report_regenerates_quoted_tables():
         for size, r in d.items():
             assert r["Auto"] <= r["NCCL"] * 1.0001, (p, size, r["Auto"], r["NCCL"])
     assert re.search(r"Smallest margin over NCCL: 1\.\d\dx", text)
+
+
+def test_public_api_names_resolve():
+    """Every name the package advertises resolves (lazily) on a CPU-only box."""
+    import results_b200 as lz
+
+    for name in lz.__all__:
+        assert getattr(lz, name) is not None, name
+    assert "allreduce" in dir(lz)
