@@ -216,11 +216,27 @@ def main():
                 consumed[k % 2].record(cs)
                 host_out.copy_(y[: host_out.numel()], non_blocking=True)
                 state["k"] = k + 1
-        else:
+        else:  # the same double-buffered pipeline around NCCL
+            xin = [x, torch.empty_like(x)]
+            copy_s = torch.cuda.Stream()
+            ready = [torch.cuda.Event(), torch.cuda.Event()]
+            consumed = [torch.cuda.Event(), torch.cuda.Event()]
+            state = {"k": 0}
+
             def e2e_step():
-                x.copy_(host_in, non_blocking=True)
-                dist.all_reduce(x)
-                host_out.copy_(x[: host_out.numel()], non_blocking=True)
+                k = state["k"]
+                buf = xin[k % 2]
+                with torch.cuda.stream(copy_s):
+                    if k >= 2:
+                        copy_s.wait_event(consumed[k % 2])
+                    buf.copy_(host_in, non_blocking=True)
+                    ready[k % 2].record(copy_s)
+                cs = torch.cuda.current_stream()
+                cs.wait_event(ready[k % 2])
+                dist.all_reduce(buf)
+                consumed[k % 2].record(cs)
+                host_out.copy_(buf[: host_out.numel()], non_blocking=True)
+                state["k"] = k + 1
 
         e_ms, _ = _timed(e2e_step, args.steps, args.warmup, ctrl, [local])
         _, e_bus = bw(e_ms)
