@@ -9,6 +9,7 @@ variant, grouped bars per configuration) are written as standalone SVG.
     python -m results_b200.utils.plots latency out.csv fig.svg # the same, time per call (log)
     python -m results_b200.utils.plots kv kv.csv fig.svg       # KV-cache transfer latency vs tokens
     python -m results_b200.utils.plots weights fig.svg a.json b.json  # weight-update bars
+    python -m results_b200.utils.plots xy in.csv fig.svg X Y SERIES [TITLE]  # any CSV
     python -m results_b200.utils.plots codec codec.csv fig.svg # schema-D codec table
 """
 from __future__ import annotations
@@ -186,6 +187,18 @@ def kv_chart(csv_path: str, svg_path: str) -> str:
                       xlabel="input tokens", ylabel="ms")
 
 
+def xy_chart(csv_path: str, svg_path: str, x: str, y: str, series: str, title: str = "",
+             ylabel: str = "") -> str:
+    """Generic line chart of one CSV: column `y` vs column `x`, one line per value of `series`."""
+    data: dict = {}
+    with open(csv_path) as f:
+        for r in csv.DictReader(f):
+            if r.get(x) in (None, "") or r.get(y) in (None, ""):
+                continue
+            data.setdefault(r[series], []).append((float(r[x]), float(r[y])))
+    return line_chart(data, svg_path, title=title, xlabel=x, ylabel=ylabel or y)
+
+
 def codec_chart(csv_path: str, svg_path: str) -> str:
     comp, dec = [], []
     with open(csv_path) as f:
@@ -198,6 +211,10 @@ def codec_chart(csv_path: str, svg_path: str) -> str:
 
 if __name__ == "__main__":
     kind, src, dst = sys.argv[1:4]
+    if kind == "xy":  # plots xy in.csv out.svg X Y SERIES [TITLE]
+        xy_chart(src, dst, sys.argv[4], sys.argv[5], sys.argv[6], title=sys.argv[7] if len(sys.argv) > 7 else "")
+        print(dst)
+        sys.exit(0)
     if kind == "weights":  # plots weights out.svg a.json b.json ...
         weight_update_chart(sys.argv[3:], src)
         print(src)
