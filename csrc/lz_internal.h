@@ -23,6 +23,18 @@ int lz_heap_world(LzHeap* h);
   } while (0)
 
 // Communicator: device-visible state plus the heap layout.
+//
+// Flag area at the start of every rank's heap (kLzFlagsBytes, zeroed at
+// creation; every protocol writes monotonic values, so nothing is reset):
+//   [0, 32K)        block barriers [LZ_MAX_BLOCKS][LZ_MAX_RANKS]      lz_common.cuh
+//   [32K, 40K)      ring ready / credit [LZ_MAX_BLOCKS]               lz_allreduce.cu
+//   [64K, 128K)     weight-transfer ready flags, p2p / broadcast        lz_weights.cu
+//   [128K, 192K)    weight-transfer credits, p2p / broadcast            lz_weights.cu
+//   [192K, 448K)    relay-broadcast barriers, one 32K region per sender lz_weights.cu
+//   [448K, 480K)    relay-broadcast chunk-ready flags, 4K per sender    lz_weights.cu
+//   [480K, 480K+128) copy-engine ready / clear-to-send                  lz_weights.cu
+//   [512K]          failure-test flag that nothing sets                 lz_allreduce.cu
+// (static_asserts next to each region keep neighbours from overlapping.)
 static constexpr size_t kLzFlagsBytes = 1 << 20;
 static constexpr size_t kLzLlMaxBytes = 256u << 10;  // largest low-latency one-shot message
 
