@@ -4,6 +4,9 @@ step and pushes them to the inference ranks, which check what they received.
     torchrun --nproc-per-node 8 -m results_b200.examples.rl_weight_sync --steps 5
     torchrun --nproc-per-node 3 -m results_b200.examples.rl_weight_sync --device cpu --layers 2
 
+With ``--resume`` the trainer restarts from the newest dumped version
+(checkpoint / resume of the weight stream).
+
 Rank 0 plays the trainer (GLM-4-9B-shaped state_dict, optionally fewer
 layers), every other rank an inference engine holding its own copy. Each step
 the trainer applies a synthetic optimizer update, then every rank calls
@@ -44,6 +47,8 @@ def main(argv=None):
     ap.add_argument("--dump-dir", default=None)
     ap.add_argument("--dump-every", type=int, default=0)
     ap.add_argument("--small", action="store_true", help="tiny shapes (tests)")
+    ap.add_argument("--resume", action="store_true",
+                    help="trainer starts from the newest version dumped in --dump-dir")
     a = ap.parse_args(argv)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -72,8 +77,19 @@ def main(argv=None):
             for k, t in sym.items():
                 t.copy_(sd[k])
             sd = sym
+    start = 1
+    if a.resume and a.dump_dir:
+        # every rank learns the version; the trainer loads its weights
+        v = [weights.latest_dump_version(a.dump_dir) if rank == 0 else None]
+        dist.broadcast_object_list(v, src=0)
+        if v[0] is not None:
+            if rank == 0:
+                back = weights.load_dump(a.dump_dir, v[0])
+                for k, t in sd.items():
+                    t.copy_(back[k].to(t.device))
+            start = v[0] + 1
     ok_all = True
-    for step in range(1, a.steps + 1):
+    for step in range(start, start + a.steps):
         if rank == 0:  # a synthetic optimizer step: every weight moves a little
             g = torch.Generator(device=dev).manual_seed(step)
             for t in sd.values():
@@ -89,7 +105,7 @@ def main(argv=None):
         dt = time.perf_counter() - t0
         dist.broadcast_object_list(want, src=0)
         ok = checksum(sd) == want[0]
-        flag = torch.tensor([0 if ok else 1])
+        flag = torch.tensor([0 if ok else 1], device=dev)  # NCCL reduces device tensors
         dist.all_reduce(flag)
         ok_all = ok_all and int(flag.item()) == 0
         if rank == 0:

@@ -515,6 +515,21 @@ def dump_tensors(named, dump_dir: str, weight_version: int, shard_idx: int, grou
     return path
 
 
+def latest_dump_version(dump_dir: str) -> int | None:
+    """Highest weight version with a manifest under `dump_dir` (None if there is none)."""
+    if not os.path.isdir(dump_dir):
+        return None
+    best = None
+    for name in os.listdir(dump_dir):
+        if name.startswith("weight_version_") and os.path.exists(os.path.join(dump_dir, name, "manifest.jsonl")):
+            try:
+                v = int(name[len("weight_version_"):])
+            except ValueError:
+                continue
+            best = v if best is None or v > best else best
+    return best
+
+
 def load_dump(dump_dir: str, weight_version: int) -> dict:
     """Read back every shard of a dumped weight version (bit-exact oracle for receivers)."""
     step_dir = os.path.join(dump_dir, f"weight_version_{weight_version:06d}")
