@@ -51,6 +51,25 @@ def allreduce_table(paths: dict) -> str:
     return "\n".join(lines)
 
 
+LINK_GBPS = 770.0  # measured peer-copy bandwidth per direction on this pool's B200s
+
+
+def roofline_table(paths: dict, size: str = "1 GB") -> str:
+    """Two-shot and NVLS at `size`: NVLink bytes per GPU per direction over the
+    measured link bandwidth, against the measured time. Two-shot moves
+    2(N-1)/N n each way; NVLS (1 + 1/N) n (switch-side reduce, multicast store)."""
+    lines = ["| algorithm | GPUs | bound (us) | measured (us) | of bound |", "|---|---|---|---|---|"]
+    n = 1 << 30 if size == "1 GB" else None
+    for w, p in sorted(paths.items()):
+        d = sweep_times(p).get(size, {})
+        for label, factor in (("P2P", 2 * (w - 1) / w), ("NVLS", 1 + 1 / w)):
+            if label in d and n:
+                bound = factor * n / (LINK_GBPS * 1e9) * 1e6
+                lines.append(f"| {'two-shot' if label == 'P2P' else 'NVLS'} | {w} | {bound:.0f} | {d[label]:.0f} | "
+                             f"{100 * bound / d[label]:.0f} % |")
+    return "\n".join(lines)
+
+
 def weight_table(paths: list) -> str:
     lines = ["| file | model | ranks | mode | s / update | GB/s per receiver | bit-exact |",
              "|---|---|---|---|---|---|---|"]
@@ -85,6 +104,7 @@ def main(argv=None) -> str:
             sweeps[int(m.group(1))] = p
     if sweeps:
         parts.append("## Allreduce (CUDA-graph device time)\n\n" + allreduce_table(sweeps))
+        parts.append("## Roofline, 1 GB (NVLink bytes per direction / 770 GB/s)\n\n" + roofline_table(sweeps))
     wj = sorted(glob.glob(os.path.join(root, "json", "weight_update_*.json")))
     if wj:
         parts.append("## Weight update\n\n" + weight_table(wj))
