@@ -670,6 +670,8 @@ static int init_comm_state(LzComm* c, int dev, size_t oneshot_bytes, size_t stag
   c->dev.epoch = reinterpret_cast<unsigned long long*>(dstate);
   c->dev.done = reinterpret_cast<unsigned int*>(dstate + 64);
   c->dev.abort_flag = reinterpret_cast<int*>(dstate + 128);
+  c->ce_seq = reinterpret_cast<unsigned long long*>(dstate + 192);
+  c->ce_done = reinterpret_cast<unsigned int*>(dstate + 224);
   int* st_host = nullptr;
   LZ_CUDA_TRY(cudaHostAlloc(&st_host, 64, cudaHostAllocMapped));
   memset(st_host, 0, 64);
@@ -720,6 +722,7 @@ extern "C" int lz_comm_create(LzHeap* h, size_t oneshot_bytes, size_t stage_byte
 }
 
 static void free_comm_state(LzComm* c) {
+  lz_ce_release(c);
   cudaFree(c->dev.epoch);
   cudaFreeHost(c->status_host);
 }

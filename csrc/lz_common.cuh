@@ -345,12 +345,12 @@ LZ_DEV unsigned long long* peer_flags(const LzDevComm& c, int peer) {
 }
 
 // CTA barrier ahead of a release signal. The signalling thread then issues
-// fence.acq_rel.sys + st.release.sys; by the PTX memory model the barrier
-// puts every thread's earlier stores in causality order before that release,
-// so they are published with it. `fence_all` (environment LZ_FENCE_ALL=1)
-// additionally makes every thread fence its own stores first: a diagnostic
-// switch for ordering questions, off by default (it costs a system-scope
-// fence per warp per signal).
+// one st.release.sys (no separate fence): by the PTX memory model the
+// bar.sync puts every thread's earlier stores in causality order before that
+// release, so they are published with it. `fence_all` (environment
+// LZ_FENCE_ALL=1) additionally makes every thread execute fence.acq_rel.sys
+// before the barrier: a diagnostic switch for ordering questions, off by
+// default (it costs a system-scope fence per warp per signal).
 LZ_DEV void publish_block_writes(const LzDevComm& c) {
   if (c.fence_all) fence_sys();
   __syncthreads();
@@ -358,7 +358,8 @@ LZ_DEV void publish_block_writes(const LzDevComm& c) {
 
 // All-pairs barrier between block `blockIdx.x` of every rank. Threads
 // 0..world-1 each own one peer. Prior stores of the whole block are released
-// (every thread fences, bar.sync, then release stores).
+// by bar.sync followed by each owning thread's st.release.sys to its peer
+// (plus a per-thread fence first only under LZ_FENCE_ALL=1).
 // Returns false (uniformly for the block) if a wait gave up.
 LZ_DEV bool block_barrier(const LzDevComm& c, unsigned long long epoch, int phase) {
   __shared__ int s_fail;

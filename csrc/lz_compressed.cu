@@ -41,6 +41,7 @@ struct CzParams {
   size_t ag_off;       // heap offset: AG slots [owner][tg]
   float* acc;          // local fp32 scratch, TG_ELEMS per CTA
   int use_mc;          // publish AG records with multimem.st
+  int hybrid;          // reduce-scatter moves raw bytes; only the all-gather is compressed
 };
 
 union CzSmem {
@@ -106,6 +107,14 @@ LZ_DEV void accumulate_plain(const char* __restrict__ in, uint32_t n, float* __r
   }
 }
 
+// Copies `bytes` from src to dst (both 16-B aligned) with the whole CTA:
+// 16-byte vectors, then the last bytes one per thread (never reads past src).
+LZ_DEV void cta_copy_bytes(char* dst, const char* src, uint32_t bytes) {
+  const uint32_t v = bytes / 16 * 16;
+  for (uint32_t o = threadIdx.x * 16; o < v; o += blockDim.x * 16) st_v4(dst + o, ld_cg_v4(src + o));
+  if (threadIdx.x < bytes - v) dst[v + threadIdx.x] = src[v + threadIdx.x];
+}
+
 template <int DT>
 LZ_DEV void store_rounded(const float* __restrict__ acc, uint32_t n, char* __restrict__ out) {
   for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
@@ -131,13 +140,16 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
   };
 
   // 1. encode my input's TGs of every peer's slice into that peer's RS slots
+  //    (hybrid: copy them raw; the reduce-scatter then pays no codec work)
   for (int k = 1; k < W; ++k) {
     const int dst = (me + k) % W;
     const uint64_t s0 = slice_begin(p, dst), sl = slice_len(p, dst);
     const uint32_t nt = ntg_of(p, dst);
     for (uint32_t t = b; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
-      encode_tg<DT>(p.in + (s0 + (uint64_t)t * TG_ELEMS) * ES, tn, rs_slot(dst, me, t), sm.enc);
+      const char* src = p.in + (s0 + (uint64_t)t * TG_ELEMS) * ES;
+      if (p.hybrid) cta_copy_bytes(rs_slot(dst, me, t), src, tn * ES);
+      else encode_tg<DT>(src, tn, rs_slot(dst, me, t), sm.enc);
     }
   }
   if (!block_barrier(c, epoch, 1)) return;
@@ -154,6 +166,8 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
       for (int s = 0; s < W; ++s) {
         if (s == me) {
           accumulate_plain<DT>(p.in + e0 * ES, tn, acc, s == 0);
+        } else if (p.hybrid) {
+          accumulate_plain<DT>(rs_slot(me, s, t), tn, acc, s == 0);
         } else {
           const char* rec = rs_slot(me, s, t);
           if (!decode_tg_syms<DT>(rec, p.cap, tn, sm.dec)) {
@@ -248,8 +262,10 @@ extern "C" size_t lz_cz_stage_bytes(size_t n, int dtype, int world, int nblocks)
 
 extern "C" int lz_cz_default_blocks(LzComm* c) { return c->sm_count * 3; }
 
+// flags: bit 0 publish the all-gather records with NVLS multimem.st (when a
+// multicast object exists), bit 1 hybrid (raw reduce-scatter).
 static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dtype, int G,
-                   int use_multicast, CzParams* out_p) {
+                   int flags, CzParams* out_p) {
   const int W = c->dev.world;
   if (dtype != LZ_F32 && dtype != LZ_F16 && dtype != LZ_BF16) {
     lz_set_error("compressed allreduce: dtype %d not supported (float types only)", dtype);
@@ -276,13 +292,16 @@ static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dty
   p.rs_off = c->stage_off;
   p.ag_off = c->stage_off + (size_t)W * p.ntg_max * p.cap;
   p.acc = reinterpret_cast<float*>(c->dev.heap[c->dev.rank] + p.ag_off + (size_t)W * p.ntg_max * p.cap);
-  p.use_mc = (use_multicast && c->dev.heap_mc) ? 1 : 0;
+  p.use_mc = ((flags & 1) && c->dev.heap_mc) ? 1 : 0;
+  p.hybrid = (flags & 2) ? 1 : 0;
   *out_p = p;
   return LZE_OK;
 }
 
+// flags: bit 0 multicast all-gather, bit 1 hybrid (raw reduce-scatter, the
+// compressed P2P hybrid of the reference's compressed_p2p_allreduce.py:54-188).
 extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, size_t n, int dtype,
-                                       int nblocks, int use_multicast, cudaStream_t s) {
+                                       int nblocks, int flags, cudaStream_t s) {
   const int W = c->dev.world;
   const size_t es = dtype == LZ_F32 ? 4 : 2;
   if (W == 1) {
@@ -292,7 +311,7 @@ extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, siz
   int G = nblocks > 0 ? nblocks : lz_cz_default_blocks(c);
   if (G > LZ_MAX_BLOCKS) G = LZ_MAX_BLOCKS;
   CzParams p;
-  int rc = cz_plan(c, in, out, n, dtype, G, use_multicast, &p);
+  int rc = cz_plan(c, in, out, n, dtype, G, flags, &p);
   if (rc) return rc;
   void* fn = cz_kernel_for(dtype, false);
   const size_t smem = sizeof(CzSmem);
@@ -304,7 +323,7 @@ extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, siz
 
 // Single-GPU emulation of the compressed allreduce over the R emulated ranks.
 extern "C" int lz_emu_compressed_allreduce(LzEmu* e, const void* const* ins, void* const* outs,
-                                           size_t n, int dtype, int nblocks, cudaStream_t s) {
+                                           size_t n, int dtype, int nblocks, int flags, cudaStream_t s) {
   const int R = lz_emu_world(e);
   void* fn = cz_kernel_for(dtype, true);
   const size_t smem = sizeof(CzSmem);
@@ -319,7 +338,7 @@ extern "C" int lz_emu_compressed_allreduce(LzEmu* e, const void* const* ins, voi
   }
   CzParams hp[LZ_MAX_RANKS];
   for (int r = 0; r < R; ++r) {
-    int rc = cz_plan(lz_emu_comm(e, r), ins[r], outs[r], n, dtype, G, 0, &hp[r]);
+    int rc = cz_plan(lz_emu_comm(e, r), ins[r], outs[r], n, dtype, G, flags & 2, &hp[r]);
     if (rc) return rc;
   }
   static_assert(sizeof(CzParams) * LZ_MAX_RANKS <= 4096, "param buffer");

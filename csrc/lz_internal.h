@@ -34,6 +34,7 @@ int lz_heap_world(LzHeap* h);
 //   [448K, 480K)    relay-broadcast chunk-ready flags, 4K per sender    lz_weights.cu
 //   [480K, 480K+128) copy-engine ready / clear-to-send                  lz_weights.cu
 //   [512K]          failure-test flag that nothing sets                 lz_allreduce.cu
+//   [544K, 562K)    copy-engine two-shot: started / done / chunk flags   lz_copy_engine.cu
 // (static_asserts next to each region keep neighbours from overlapping.)
 static constexpr size_t kLzFlagsBytes = 1 << 20;
 static constexpr size_t kLzLlMaxBytes = 256u << 10;  // largest low-latency one-shot message
@@ -52,7 +53,17 @@ struct LzComm {
   size_t user_off;        // start of the user-allocatable region
   int sm_count;
   int* status_host;       // host view of dev.status
+  // copy-engine allreduce (lz_copy_engine.cu): call counter and finished-block
+  // counter in device memory, plus side streams and events created on first use
+  unsigned long long* ce_seq;
+  unsigned int* ce_done;
+  cudaStream_t ce_stream[3];
+  cudaEvent_t* ce_events;
+  int ce_nevents;
 };
+
+// Releases the copy-engine streams and events of a communicator (if created).
+void lz_ce_release(LzComm* c);
 
 // Returns the heap offset of [p, p+bytes) when it lies in this rank's heap, or
 // (size_t)-1.

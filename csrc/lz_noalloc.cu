@@ -46,7 +46,7 @@ int scratch_for_current_device(void** out) {
 }  // namespace
 
 extern "C" size_t lz_codec_noalloc_max_elems(int dtype) {
-  if (dtype < lzc::DT_F32 || dtype > lzc::DT_U8) return 0;
+  if (!lzc::valid_dtype(dtype)) return 0;
   // largest table-group count whose scratch fits, times the group size
   size_t lo = 0, hi = (size_t)LZ_NOALLOC_SCRATCH_BYTES / 16 + 1;
   while (hi - lo > 1) {
@@ -60,7 +60,7 @@ extern "C" size_t lz_codec_noalloc_max_elems(int dtype) {
 extern "C" int lz_codec_encode_noalloc(const void* in, size_t n, int dtype, void* out,
                                        size_t out_cap, unsigned long long* d_total,
                                        cudaStream_t stream) {
-  if (dtype < lzc::DT_F32 || dtype > lzc::DT_U8) {
+  if (!lzc::valid_dtype(dtype)) {
     lz_set_error("noalloc encoder: unsupported dtype %d", dtype);
     return LZE_ARG;
   }

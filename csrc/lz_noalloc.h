@@ -26,7 +26,10 @@
 //     has to start at zero. Calls whose executions overlap on the GPU (e.g. on
 //     two streams without ordering between them) race on the array: order
 //     them on one stream or serialise them.
-//   * Output is byte-identical to lz_codec_encode() with caller scratch.
+//   * Every dtype of lz_codec_encode() is accepted (fp32, fp16, bf16, bytes
+//     and the packed fp8 pair containers e4m3 / e5m2, whose element count is
+//     the number of pairs); output is byte-identical to lz_codec_encode()
+//     with caller scratch.
 #pragma once
 #include <stddef.h>
 #include <cuda_runtime.h>

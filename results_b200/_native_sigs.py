@@ -22,6 +22,9 @@ _CUDA = {
 }
 
 _CUDA["lz_test_wait_timeout"] = (c_int, c_ptr, c_dbl, c_ptr)
+# copy-engine allreduce (csrc/lz_copy_engine.cu)
+_CUDA["lz_ce_allreduce"] = (c_int, c_ptr, c_ptr, c_ptr, c_size, c_int, c_int, c_ptr)
+_CUDA["lz_ce_allreduce_is_zero_copy"] = (c_int, c_ptr, c_ptr, c_ptr, c_size, c_int)
 _CUDA["lz_emu_weight_transfer"] = (c_int, c_ptr, c_int, c_u32, P(c_ptr), c_u32, c_int, c_int, c_int,
                                    P(c_u64), c_ptr)
 

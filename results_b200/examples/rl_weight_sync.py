@@ -97,6 +97,7 @@ def main(argv=None):
                     t.add_((torch.randn(t.shape, generator=g, device=dev) * 1e-3).to(t.dtype))
             if a.dump_dir and a.dump_every and step % a.dump_every == 0:
                 weights.dump_tensors(list(sd.items()), a.dump_dir, step, 0, group_name="trainer")
+                weights.mark_dump_complete(a.dump_dir, step, 1)
         want = [checksum(sd) if rank == 0 else None]
         t0 = time.perf_counter()
         weights.broadcast_weights(sd, src=0, comm=comm, mode=a.mode)

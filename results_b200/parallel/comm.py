@@ -153,15 +153,22 @@ class Communicator:
     def reset_alloc(self) -> None:
         self._bump = self._user_off
 
-    def tensor_at(self, offset: int, shape, dtype: torch.dtype, rank: int | None = None) -> torch.Tensor:
-        """Tensor view of heap memory of ``rank`` (default: this rank) at ``offset``."""
+    def tensor_at(self, offset: int, shape, dtype: torch.dtype) -> torch.Tensor:
+        """Tensor view of this rank's own heap memory at ``offset``.
+
+        There is deliberately no way to get a torch view of a peer's heap:
+        only this library's kernels and copy-engine transfers touch peer
+        memory, never a PyTorch or other library kernel.
+        """
         shape = tuple(shape) if isinstance(shape, (tuple, list, torch.Size)) else (int(shape),)
         numel = 1
         for s in shape:
             numel *= int(s)
         nbytes = numel * torch.empty((), dtype=dtype).element_size()
-        base = self._local_base if rank is None else self._lib.lz_heap_ptr(self._heap, rank)
-        buf = _CudaBuf(base + offset, max(nbytes, 1), self)
+        if offset < self._user_off or offset + nbytes > self.heap_bytes:
+            raise ValueError(f"heap range [{offset}, {offset + nbytes}) is outside the user region "
+                             f"[{self._user_off}, {self.heap_bytes})")
+        buf = _CudaBuf(self._local_base + offset, max(nbytes, 1), self)
         t = torch.as_tensor(buf, device=f"cuda:{self.device}")[:nbytes]
         return t.view(dtype).view(shape)
 
@@ -181,15 +188,27 @@ class Communicator:
 
     # ------------------------------------------------------------ collectives
     def allreduce_(self, inp: torch.Tensor, out: torch.Tensor | None = None, algo: str = "twoshot",
-                   nblocks: int = 0, nthreads: int = 0, stream=None) -> torch.Tensor:
-        """Native sum-allreduce of a contiguous CUDA tensor (in place by default)."""
+                   nblocks: int = 0, nthreads: int = 0, stream=None, pipes: int = 0) -> torch.Tensor:
+        """Native sum-allreduce of a contiguous CUDA tensor (in place by default).
+
+        ``algo="ce"`` is the copy-engine two-shot (``pipes`` chunks per slice,
+        0 = automatic); every other algorithm is one kernel launch.
+        """
         if out is None:
             out = inp
         if not (inp.is_contiguous() and out.is_contiguous()):
             raise ValueError("allreduce needs contiguous tensors")
         if inp.numel() != out.numel() or inp.dtype != out.dtype:
             raise ValueError("input and output must match in numel and dtype")
+        for t in (inp, out):
+            if not t.is_cuda or t.device.index != self.device:
+                raise ValueError(f"allreduce tensors must be on cuda:{self.device} (got {t.device})")
         s = stream or torch.cuda.current_stream(self.device)
+        if algo == "ce":
+            rc = self._lib.lz_ce_allreduce(self._comm, inp.data_ptr(), out.data_ptr(), inp.numel(),
+                                           lz_dtype(inp.dtype), int(pipes), s.cuda_stream)
+            _native.check(rc, "allreduce[ce]")
+            return out
         nb = nblocks or self.config.sm_budget
         nt = nthreads or self.config.nthreads
         rc = self._lib.lz_allreduce(self._comm, inp.data_ptr(), out.data_ptr(), inp.numel(),

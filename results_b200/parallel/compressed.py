@@ -44,7 +44,7 @@ _native_sigs.add_cuda({
     "lz_compressed_allreduce": (C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_int,
                                 C.c_int, C.c_void_p),
     "lz_emu_compressed_allreduce": (C.c_int, C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
-                                    C.c_size_t, C.c_int, C.c_int, C.c_void_p),
+                                    C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_void_p),
 })
 
 HDR = 16  # u64 stream size + u64 overflow flag
@@ -57,8 +57,15 @@ def stage_bytes_needed(n: int, dtype: torch.dtype, world: int, nblocks: int = 44
 
 @traced("compressed_allreduce")
 def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=None,
-                         nblocks: int = 0, multicast: bool = True, stream=None) -> torch.Tensor:
-    """Sum-allreduce with lossless compression on the wire (native fused kernel)."""
+                         nblocks: int = 0, multicast: bool = True, stream=None,
+                         hybrid: bool = False) -> torch.Tensor:
+    """Sum-allreduce with lossless compression on the wire (native fused kernel).
+
+    ``hybrid=True`` is the compressed P2P hybrid: the reduce-scatter moves raw
+    bytes and only the all-gather of the reduced slices is compressed, so each
+    GPU encodes 1/W of the vector instead of all of it
+    (single_node_nccl_allreduce_benchmark/compressed_p2p_allreduce.py:54-188 of the reference).
+    """
     from .allreduce import get_comm, init
 
     if not t.is_cuda:
@@ -69,7 +76,8 @@ def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=
     s = stream or torch.cuda.current_stream(comm.device)
     nb = nblocks or comm.config.sm_budget
     rc = comm._lib.lz_compressed_allreduce(comm.handle, t.data_ptr(), out.data_ptr(), t.numel(),
-                                           lz_dtype(t.dtype), nb, int(multicast), s.cuda_stream)
+                                           lz_dtype(t.dtype), nb, int(multicast) | (2 if hybrid else 0),
+                                           s.cuda_stream)
     _native.check(rc, "compressed_allreduce")
     return out
 

@@ -1,8 +1,11 @@
 """Allreduce paths that move data without SM copy loops.
 
-* :func:`ce_allreduce` -- two-shot whose peer reads are copy-engine DMA
-  (cudaMemcpyAsync from peer-mapped heap memory) pipelined over ``pipes``
-  pieces on a second stream; SMs only accumulate (csrc/lz_copy_engine.cu).
+* :func:`ce_allreduce` -- two-shot whose bytes cross NVLink by copy-engine
+  DMA (cudaMemcpyAsync into / from peer-mapped heap memory) while the SMs only
+  accumulate (csrc/lz_copy_engine.cu). Symmetric, distinct input and output
+  take the zero-copy pipelined path (reduce-scatter pushes, per-chunk reduce,
+  all-gather pushes on two side streams, ``pipes`` chunks per slice, 0 =
+  automatic); other buffers go through the communicator stage.
 * :func:`hoststaged_allreduce` -- PCIe emulation: every exchange goes
   through pinned, cross-process shared host memory (D2H, host barrier, H2D),
   the B200 counterpart of the reference's host-staged mode and of its
@@ -12,34 +15,27 @@
 """
 from __future__ import annotations
 
-import ctypes as C
 from multiprocessing import shared_memory
 
 import torch
 import torch.distributed as dist
 
-from .. import _native, _native_sigs
 from ..utils.dtypes import lz_dtype
 
-_native_sigs.add_cuda({
-    "lz_ce_allreduce": (C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p,
-                        C.c_void_p),
-})
 
-_STREAMS: dict = {}
-
-
-def ce_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=None, pipes: int = 4) -> torch.Tensor:
+def ce_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=None, pipes: int = 0) -> torch.Tensor:
+    """Copy-engine two-shot sum-allreduce (in place unless ``out`` is given)."""
     from .allreduce import get_comm, init
 
     comm = comm or get_comm() or init()
+    return comm.allreduce_(t, out, algo="ce", pipes=pipes)
+
+
+def is_zero_copy(comm, t: torch.Tensor, out: torch.Tensor | None = None) -> bool:
+    """True when (t, out) take the zero-copy pipelined copy-engine path."""
     out = t if out is None else out
-    s = torch.cuda.current_stream(comm.device)
-    s2 = _STREAMS.setdefault(comm.device, torch.cuda.Stream(comm.device))
-    rc = comm._lib.lz_ce_allreduce(comm.handle, t.data_ptr(), out.data_ptr(), t.numel(), lz_dtype(t.dtype),
-                                   pipes, s.cuda_stream, s2.cuda_stream)
-    _native.check(rc, "copy-engine allreduce")
-    return out
+    return bool(comm._lib.lz_ce_allreduce_is_zero_copy(comm.handle, t.data_ptr(), out.data_ptr(), t.numel(),
+                                                        lz_dtype(t.dtype)))
 
 
 class _HostStage:

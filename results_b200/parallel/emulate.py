@@ -62,14 +62,14 @@ class EmulatedWorld:
                                         s.cuda_stream)
         _native.check(rc, f"emulated allreduce[{algo}]")
 
-    def compressed_allreduce(self, ins, outs, nblocks: int = 0):
+    def compressed_allreduce(self, ins, outs, nblocks: int = 0, hybrid: bool = False):
         from . import compressed  # noqa: F401  (declares the native signature)
 
         R = self.world
         arr_in = (C.c_void_p * R)(*[t.data_ptr() for t in ins])
         arr_out = (C.c_void_p * R)(*[t.data_ptr() for t in outs])
         rc = self._lib.lz_emu_compressed_allreduce(self._emu, arr_in, arr_out, ins[0].numel(),
-                                                   lz_dtype(ins[0].dtype), nblocks,
+                                                   lz_dtype(ins[0].dtype), nblocks, 2 if hybrid else 0,
                                                    torch.cuda.current_stream().cuda_stream)
         _native.check(rc, "emulated compressed allreduce")
 

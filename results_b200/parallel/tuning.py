@@ -54,11 +54,16 @@ TABLE = {
 }
 
 
-def choose(nbytes: int, world: int, has_multicast: bool, symmetric: bool) -> str:
+def choose(nbytes: int, world: int, has_multicast: bool, symmetric: bool, out_of_place: bool = True) -> str:
+    """Row of TABLE for (world, nbytes). The copy-engine two-shot ("ce") is
+    zero-copy only for symmetric, distinct input and output; otherwise the
+    two-shot kernel takes its rows."""
     rows = TABLE.get(world, TABLE["default"])
     for max_b, with_mc, without_mc in rows:
         if nbytes <= max_b:
             algo = with_mc if has_multicast else without_mc
+            if algo == "ce" and not (symmetric and out_of_place and nbytes % (16 * world) == 0):
+                algo = "twoshot"
             if nbytes % 16 and algo != "oneshot":
                 return "oneshot" if nbytes <= 4 * MiB else "twoshot"
             return algo

@@ -423,12 +423,16 @@ def send_weights(state_dict, dst, comm=None, mode: str = "split_ans", bucket_byt
     bb = bucket_bytes or eng.comm.config.update_weight_buffer_bytes
     me = dist.get_rank() if isinstance(eng, HostTransfer) else eng.comm.rank
     trace.log.info("[START] send_weights version=%d mode=%s dst=%s", weight_version, mode, dst)
+    nb = 0
     for i, bucket in enumerate(_progress(list(buckets(list(state_dict.items()), bb)), "send_weights")):
         _log_bucket("send", i, bucket)
         if dump_dir:
             dump_tensors(bucket, dump_dir, weight_version, i, group_name=f"src{me}")
         with trace.range(f"send_weights.bucket{i}"):
             eng.send([t for _, t in bucket], dst)
+        nb = i + 1
+    if dump_dir:
+        mark_dump_complete(dump_dir, weight_version, nb)
 
 
 def recv_weights(state_dict, src: int, comm=None, mode: str = "split_ans", bucket_bytes: int | None = None,
@@ -515,17 +519,54 @@ def dump_tensors(named, dump_dir: str, weight_version: int, shard_idx: int, grou
     return path
 
 
+COMPLETE_MARKER = "COMPLETE.json"
+
+
+def mark_dump_complete(dump_dir: str, weight_version: int, num_shards: int) -> str:
+    """Record that every shard of a version is written (written last, after
+    the final manifest line, through a rename so it appears atomically)."""
+    step_dir = os.path.join(dump_dir, f"weight_version_{weight_version:06d}")
+    os.makedirs(step_dir, exist_ok=True)
+    path = os.path.join(step_dir, COMPLETE_MARKER)
+    tmp = path + f".tmp{os.getpid()}"
+    with open(tmp, "w", encoding="utf-8") as f:
+        json.dump({"weight_version": int(weight_version), "num_shards": int(num_shards), "time": time.time()}, f)
+    os.replace(tmp, path)
+    return path
+
+
+def _dump_complete(step_dir: str) -> bool:
+    """A version counts only when its marker exists and the manifest lists as
+    many distinct shards as the marker promises (a crash part-way through a
+    multi-shard dump leaves no marker, or a short manifest)."""
+    try:
+        with open(os.path.join(step_dir, COMPLETE_MARKER), encoding="utf-8") as f:
+            want = int(json.load(f)["num_shards"])
+        shards = set()
+        with open(os.path.join(step_dir, "manifest.jsonl"), encoding="utf-8") as f:
+            for line in f:
+                if line.strip():
+                    shards.add(json.loads(line)["shard"])
+    except (OSError, ValueError, KeyError):
+        return False
+    return len(shards) >= want and all(os.path.exists(os.path.join(step_dir, s)) for s in shards)
+
+
 def latest_dump_version(dump_dir: str) -> int | None:
-    """Highest weight version with a manifest under `dump_dir` (None if there is none)."""
+    """Highest weight version under `dump_dir` whose dump completed (None if
+    there is none): incomplete versions are skipped, so a resume never picks
+    a dump that a crash cut short."""
     if not os.path.isdir(dump_dir):
         return None
     best = None
     for name in os.listdir(dump_dir):
-        if name.startswith("weight_version_") and os.path.exists(os.path.join(dump_dir, name, "manifest.jsonl")):
-            try:
-                v = int(name[len("weight_version_"):])
-            except ValueError:
-                continue
+        if not name.startswith("weight_version_"):
+            continue
+        try:
+            v = int(name[len("weight_version_"):])
+        except ValueError:
+            continue
+        if _dump_complete(os.path.join(dump_dir, name)):
             best = v if best is None or v > best else best
     return best
 

@@ -52,6 +52,11 @@ def write_rows(path: str, header: list[str], rows: list[dict], blocks: list[list
 
 
 def git_sha() -> str | None:
+    """HEAD of the source tree; LZ_GIT_SHA overrides it (a copy of the tree
+    without its .git directory, e.g. on a remote benchmark machine)."""
+    env = os.environ.get("LZ_GIT_SHA")
+    if env:
+        return env
     try:
         return subprocess.check_output(["git", "rev-parse", "HEAD"], stderr=subprocess.DEVNULL,
                                        cwd=os.path.dirname(os.path.abspath(__file__))).decode().strip()

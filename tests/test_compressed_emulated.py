@@ -30,15 +30,17 @@ def _inputs(R, n, dtype, seed, kind="grad"):
     return xs
 
 
+@pytest.mark.parametrize("hybrid", [False, True])
 @pytest.mark.parametrize("R", [2, 4])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-@pytest.mark.parametrize("n", [16, 1000, 32768 * 3 + 48, 400_000])
-def test_compressed_allreduce_bitexact(worlds, R, dtype, n):
+@pytest.mark.parametrize("n", [16, 1000, 32768 * 3 + 48, 400_000, 400_001])
+def test_compressed_allreduce_bitexact(worlds, R, dtype, n, hybrid):
+    """hybrid=True: raw reduce-scatter, compressed all-gather."""
     w = worlds[R]
     xs = _inputs(R, n, dtype, seed=n + R)
     outs = [torch.empty_like(x) for x in xs]
     for _ in range(2):
-        w.compressed_allreduce(xs, outs, nblocks=8)
+        w.compressed_allreduce(xs, outs, nblocks=8, hybrid=hybrid)
     torch.cuda.synchronize()
     acc = xs[0].float().clone()
     for x in xs[1:]:

@@ -52,6 +52,23 @@ def test_dump_manifest_roundtrip(tmp_path):
     assert torch.equal(back["a.weight"].view(torch.int16), named[0][1].view(torch.int16))
 
 
+def test_resume_skips_versions_whose_dump_did_not_complete(tmp_path):
+    """A multi-shard dump cut short (no completion marker, or fewer shards
+    than it promised) is never the version a resume picks."""
+    d = str(tmp_path)
+    t = [("w", torch.randn(4))]
+    weights.dump_tensors(t, d, 1, 0)
+    weights.dump_tensors(t, d, 1, 1)
+    weights.mark_dump_complete(d, 1, 2)
+    assert weights.latest_dump_version(d) == 1
+    weights.dump_tensors(t, d, 2, 0)  # crash before shard 1 and the marker
+    assert weights.latest_dump_version(d) == 1
+    weights.mark_dump_complete(d, 2, 2)  # marker promising a shard the manifest lacks
+    assert weights.latest_dump_version(d) == 1
+    weights.dump_tensors(t, d, 2, 1)
+    assert weights.latest_dump_version(d) == 2
+
+
 def test_engine_cache_is_per_communicator_object():
     """Engines are cached per communicator object (not per id(), which a new
     communicator can reuse) and released with it."""

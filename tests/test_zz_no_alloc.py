@@ -58,6 +58,30 @@ def test_noalloc_matches_allocating_encoder_two_calls():
         assert torch.equal(y.view(torch.uint8), x.view(torch.uint8))
 
 
+def test_noalloc_fp8_pair_dtypes_match_allocating_encoder():
+    from results_b200.ops import codec
+
+    lib, f, maxel = _noalloc_symbol()
+    for name, seed in (("float8_e4m3fn", 21), ("float8_e5m2", 22)):
+        fp8 = getattr(torch, name, None)
+        if fp8 is None:
+            continue
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        x = (torch.randn(2 * 700_001, device="cuda", generator=g) * 0.05).to(fp8)
+        dt, n = codec.plan(x.dtype, x.numel())
+        assert dt in (codec.DT_E4M3P, codec.DT_E5M2P) and maxel(dt) > n
+        for _ in range(2):
+            out = torch.empty(lib.lz_codec_max_bytes(n, dt), dtype=torch.uint8, device="cuda")
+            total = torch.zeros(1, dtype=torch.int64, device="cuda")
+            rc = f(x.view(torch.uint8).data_ptr(), n, dt, out.data_ptr(), out.numel(), total.data_ptr(),
+                   torch.cuda.current_stream().cuda_stream)
+            assert rc == 0, lib.lz_last_error().decode()
+            torch.cuda.synchronize()
+            got = out[: int(total.item())]
+            ref = codec.encode(x)
+            assert torch.equal(got, ref), f"noalloc {name} stream differs from lz_codec_encode"
+
+
 def test_noalloc_rejects_inputs_beyond_the_fixed_scratch():
     from results_b200.ops import codec
 
