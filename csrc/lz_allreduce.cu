@@ -265,43 +265,49 @@ __device__ __forceinline__ void nvls_body(const LzDevComm& c, const ArParams& P)
   const unsigned long long epoch = epoch_read(c);
   const int W = c.world, me = c.rank, G = gridDim.x, b = blockIdx.x;
   const size_t nv = bytes / 16;
+  // Block b owns the vectors b*T + t (mod G*T) of every slice: grid-stride
+  // interleaving measured 7 % faster than contiguous per-block pieces for the
+  // multimem loop (4 x B200, 1 GiB: 2.32 vs 2.50 ms). Copy-in, reduction and
+  // copy-out use the same mapping, so block b's barrier covers exactly the
+  // vectors its peers' blocks b touch.
+  const size_t stride = (size_t)G * blockDim.x;
   if (copy_in) {
-    // my piece of every slice goes into the stage (that is what peers' block b reads)
     for (int p = 0; p < W; ++p) {
-      Range rg = slice_piece(nv, W, p, G, b);
-      copy_vecs<false>(reinterpret_cast<uint4*>(c.heap[me] + in_off) + rg.begin,
-                       reinterpret_cast<const uint4*>(in) + rg.begin, rg.len);
+      const size_t s0 = part_begin(nv, W, p), s1 = part_begin(nv, W, p + 1);
+      uint4* dst = reinterpret_cast<uint4*>(c.heap[me] + in_off);
+      const uint4* src = reinterpret_cast<const uint4*>(in);
+      for (size_t i = s0 + (size_t)b * blockDim.x + threadIdx.x; i < s1; i += stride) dst[i] = ld_nc_v4(src + i);
     }
   }
   if (!block_barrier_mc(c, epoch, 1)) return;
   {
-    Range rg = slice_piece(nv, W, me, G, b);
-    const uint4* src = reinterpret_cast<const uint4*>(c.heap_mc + in_off) + rg.begin;
-    uint4* dst = reinterpret_cast<uint4*>(c.heap_mc + out_off) + rg.begin;
+    const size_t s0 = part_begin(nv, W, me), s1 = part_begin(nv, W, me + 1);
+    const uint4* src = reinterpret_cast<const uint4*>(c.heap_mc + in_off);
+    uint4* dst = reinterpret_cast<uint4*>(c.heap_mc + out_off);
     // P.c: loads in flight per thread (1..8); P.d bit 0: bf16 accumulation in the switch
     const int U = P.c >= 1 && P.c <= 8 ? (int)P.c : kUnroll;
     const bool noacc = (DT == LZ_BF16) && (P.d & 1);
-    const size_t stride = (size_t)blockDim.x * U;
-    size_t i = threadIdx.x;
-    for (; i + (U - 1) * blockDim.x < rg.len; i += stride) {
+    size_t i = s0 + (size_t)b * blockDim.x + threadIdx.x;
+    for (; i + (U - 1) * stride < s1; i += U * stride) {
       uint4 v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
         if (u < U)
-          v[u] = noacc ? multimem_ld_reduce_bf16_noacc(src + i + u * blockDim.x)
-                       : multimem_ld_reduce_v4<DT>(src + i + u * blockDim.x);
+          v[u] = noacc ? multimem_ld_reduce_bf16_noacc(src + i + u * stride)
+                       : multimem_ld_reduce_v4<DT>(src + i + u * stride);
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (u < U) multimem_st_v4(dst + i + u * blockDim.x, v[u]);
+        if (u < U) multimem_st_v4(dst + i + u * stride, v[u]);
     }
-    for (; i < rg.len; i += blockDim.x) multimem_st_v4(dst + i, multimem_ld_reduce_v4<DT>(src + i));
+    for (; i < s1; i += stride) multimem_st_v4(dst + i, multimem_ld_reduce_v4<DT>(src + i));
   }
   if (!block_barrier_mc(c, epoch, 2)) return;
   if (copy_out) {
     for (int p = 0; p < W; ++p) {
-      Range rg = slice_piece(nv, W, p, G, b);
-      copy_vecs<false>(reinterpret_cast<uint4*>(out) + rg.begin,
-                       reinterpret_cast<const uint4*>(c.heap[me] + out_off) + rg.begin, rg.len);
+      const size_t s0 = part_begin(nv, W, p), s1 = part_begin(nv, W, p + 1);
+      const uint4* src = reinterpret_cast<const uint4*>(c.heap[me] + out_off);
+      uint4* dst = reinterpret_cast<uint4*>(out);
+      for (size_t i = s0 + (size_t)b * blockDim.x + threadIdx.x; i < s1; i += stride) dst[i] = ld_cg_v4(src + i);
     }
   }
   epoch_advance(c);

@@ -308,6 +308,27 @@ LZ_DEV bool lz_wait_ge(const LzDevComm& c, const unsigned long long* flag,
   return false;
 }
 
+// Waits until *flag == target exactly (bounded like lz_wait_ge). For flags
+// that live inside reused data areas (slot footers), where a stale word may
+// hold any bit pattern and only an exact match may count.
+LZ_DEV bool lz_wait_eq(const LzDevComm& c, const unsigned long long* flag,
+                       unsigned long long target, int phase, int peer) {
+  if (ld_acquire_sys(flag) == target) return true;
+  const unsigned long long t0 = globaltimer();
+  for (unsigned int it = 1; it < (1u << 30); ++it) {
+    if (ld_acquire_sys(flag) == target) return true;
+    if ((it & 255u) == 0u) {
+      if (ld_volatile_i32(c.abort_flag)) return false;
+      if (globaltimer() - t0 > c.timeout_ns) {
+        lz_report(c, LZ_ERR_TIMEOUT, phase, peer);
+        return false;
+      }
+    }
+  }
+  lz_report(c, LZ_ERR_TIMEOUT, phase, peer);
+  return false;
+}
+
 #ifndef LZ_BOUNDS
 #define LZ_BOUNDS 0
 #endif

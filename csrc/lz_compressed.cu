@@ -1,7 +1,9 @@
 // Lossless compressed allreduce, fused with the NVLink transfer.
 //
-// One persistent launch per call, three phases separated by per-CTA
-// all-pairs flag barriers (bounded waits):
+// One persistent launch per call: one start barrier between same-index CTAs
+// of all ranks, then three phases linked by per-record flags (no barrier
+// between phases, so a CTA decodes and reduces its table groups while other
+// CTAs are still encoding theirs; bounded waits):
 //   1. RS encode+push: every table group (TG) of every peer's slice is
 //      split + rANS-encoded by this GPU and the record is written straight
 //      into the peer's receive slot (peer stores over NVLink): only the
@@ -15,6 +17,14 @@
 //   3. AG decode: every rank decodes the W-1 published records of the other
 //      slices straight into its output.
 // Records are never truncated: a TG that does not compress is stored RAW.
+// Every slot is followed by a 16-byte footer whose first word is the slot's
+// ready flag: the call epoch mixed with a 64-bit constant, stored with release
+// semantics after the CTA's record stores and matched exactly (the stage is
+// shared with other algorithms, so a footer may hold stale data of any
+// value; a small integer or all-zero word can never match). Table group t is always handled by CTA t mod G on every
+// rank, so the start barrier of CTA b (every rank's CTA b has finished the
+// previous call) is what keeps a new call from overwriting slots the
+// previous one still reads.
 //
 // Reference behaviour being re-designed: the compressed two-shot all-to-all
 // ("LZip two-shot", single_node_nccl_allreduce_benchmark/compressed_twoshot_allreduce.py:126-247),
@@ -37,6 +47,7 @@ struct CzParams {
   uint64_t slice;      // elements per slice (multiple of 16); slice p = [p*slice, ...)
   uint32_t ntg_max;    // TGs per slice (max)
   uint32_t cap;        // TG record capacity
+  uint32_t sstride;    // slot stride: cap + 16-byte flag footer
   size_t rs_off;       // heap offset: RS slots [src][tg]
   size_t ag_off;       // heap offset: AG slots [owner][tg]
   float* acc;          // local fp32 scratch, TG_ELEMS per CTA
@@ -133,11 +144,22 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
   const unsigned long long epoch = epoch_read(c);
   const int W = c.world, me = c.rank, G = gridDim.x, b = blockIdx.x;
   auto rs_slot = [&](int rank_heap, int src, uint32_t t) {
-    return c.heap[rank_heap] + p.rs_off + ((size_t)src * p.ntg_max + t) * p.cap;
+    return c.heap[rank_heap] + p.rs_off + ((size_t)src * p.ntg_max + t) * p.sstride;
   };
   auto ag_slot = [&](char* base, int owner, uint32_t t) {
-    return base + p.ag_off + ((size_t)owner * p.ntg_max + t) * p.cap;
+    return base + p.ag_off + ((size_t)owner * p.ntg_max + t) * p.sstride;
   };
+  auto flag_of = [&](char* slot) { return reinterpret_cast<unsigned long long*>(slot + p.cap); };
+  const unsigned long long ready = (epoch + 1ull) ^ 0x9E3779B97F4A7C15ull;
+  __shared__ int s_wfail;
+  // CTA-wide bounded wait for a slot flag (thread 0 polls)
+  auto wait_slot = [&](char* slot, int phase, int peer) {
+    if (threadIdx.x == 0) s_wfail = lz_wait_eq(c, flag_of(slot), ready, phase, peer) ? 0 : 1;
+    __syncthreads();
+    return s_wfail == 0;
+  };
+  // every rank's CTA b has finished the previous call
+  if (!block_barrier(c, epoch, 1)) return;
 
   // 1. encode my input's TGs of every peer's slice into that peer's RS slots
   //    (hybrid: copy them raw; the reduce-scatter then pays no codec work)
@@ -148,11 +170,13 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
     for (uint32_t t = b; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
       const char* src = p.in + (s0 + (uint64_t)t * TG_ELEMS) * ES;
-      if (p.hybrid) cta_copy_bytes(rs_slot(dst, me, t), src, tn * ES);
-      else encode_tg<DT>(src, tn, rs_slot(dst, me, t), sm.enc);
+      char* slot = rs_slot(dst, me, t);
+      if (p.hybrid) cta_copy_bytes(slot, src, tn * ES);
+      else encode_tg<DT>(src, tn, slot, sm.enc);
+      publish_block_writes(c);
+      if (threadIdx.x == 0) st_release_sys(flag_of(slot), ready);
     }
   }
-  if (!block_barrier(c, epoch, 1)) return;
 
   // 2. decode + reduce (rank order, fp32) + store + re-encode + publish
   {
@@ -166,6 +190,8 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
       for (int s = 0; s < W; ++s) {
         if (s == me) {
           accumulate_plain<DT>(p.in + e0 * ES, tn, acc, s == 0);
+        } else if (!wait_slot(rs_slot(me, s, t), 2, s)) {
+          return;
         } else if (p.hybrid) {
           accumulate_plain<DT>(rs_slot(me, s, t), tn, acc, s == 0);
         } else {
@@ -187,21 +213,24 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
         char* mc = ag_slot(c.heap_mc, me, t);
         for (uint32_t o = threadIdx.x * 16; o < padded; o += blockDim.x * 16)
           multimem_st_v4(mc + o, ld_cg_v4(mine + o));
+        publish_block_writes(c);
+        if (threadIdx.x == 0) {
+          fence_sys();
+          multimem_st_release_u64(flag_of(mc), ready);
+        }
       } else {
         for (int k = 1; k < W; ++k) {
           char* dstp = ag_slot(c.heap[(me + k) % W], me, t);
           for (uint32_t o = threadIdx.x * 16; o < padded; o += blockDim.x * 16)
             st_v4(dstp + o, ld_cg_v4(mine + o));
         }
+        publish_block_writes(c);
+        if (threadIdx.x == 0)
+          for (int k = 1; k < W; ++k) st_release_sys(flag_of(ag_slot(c.heap[(me + k) % W], me, t)), ready);
       }
       __syncthreads();
     }
     (void)s_bad;
-  }
-  if (p.use_mc) {
-    if (!block_barrier_mc(c, epoch, 2)) return;
-  } else {
-    if (!block_barrier(c, epoch, 2)) return;
   }
 
   // 3. decode the other owners' reduced TGs into my output
@@ -211,6 +240,8 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
     const uint32_t nt = ntg_of(p, own);
     for (uint32_t t = b; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
+      if (!wait_slot(ag_slot(c.heap[me], own, t), 3, own)) return;
+      if (p.use_mc) fence_proxy_alias();  // the record arrived through the multicast mapping
       if (!decode_tg<DT>(ag_slot(c.heap[me], own, t), p.cap, tn, p.out + (s0 + (uint64_t)t * TG_ELEMS) * ES,
                          sm.dec)) {
         if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 3, own);
@@ -256,8 +287,8 @@ void* cz_kernel_for(int dtype, bool emu) {
 extern "C" size_t lz_cz_stage_bytes(size_t n, int dtype, int world, int nblocks) {
   const uint64_t slice = ((n + world - 1) / world + 15) / 16 * 16;
   const uint64_t ntg = num_tgs(slice);
-  const uint64_t cap = tg_capacity(dtype);
-  return 2 * (size_t)world * ntg * cap + (size_t)nblocks * TG_ELEMS * 4 + 256;
+  const uint64_t sstride = tg_capacity(dtype) + 16;  // record capacity + flag footer
+  return 2 * (size_t)world * ntg * sstride + (size_t)nblocks * TG_ELEMS * 4 + 256;
 }
 
 extern "C" int lz_cz_default_blocks(LzComm* c) { return c->sm_count * 3; }
@@ -283,6 +314,7 @@ static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dty
   p.slice = ((n + W - 1) / W + 15) / 16 * 16;
   p.ntg_max = (uint32_t)num_tgs(p.slice);
   p.cap = tg_capacity(dtype);
+  p.sstride = p.cap + 16;
   const size_t need = lz_cz_stage_bytes(n, dtype, W, G);
   if (need > c->stage_bytes) {
     lz_set_error("compressed allreduce: stage needs %zu bytes, communicator has %zu (raise stage_bytes)",
@@ -290,8 +322,8 @@ static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dty
     return LZE_ARG;
   }
   p.rs_off = c->stage_off;
-  p.ag_off = c->stage_off + (size_t)W * p.ntg_max * p.cap;
-  p.acc = reinterpret_cast<float*>(c->dev.heap[c->dev.rank] + p.ag_off + (size_t)W * p.ntg_max * p.cap);
+  p.ag_off = c->stage_off + (size_t)W * p.ntg_max * p.sstride;
+  p.acc = reinterpret_cast<float*>(c->dev.heap[c->dev.rank] + p.ag_off + (size_t)W * p.ntg_max * p.sstride);
   p.use_mc = ((flags & 1) && c->dev.heap_mc) ? 1 : 0;
   p.hybrid = (flags & 2) ? 1 : 0;
   *out_p = p;

@@ -39,7 +39,6 @@
 // and host-staged pipelines, bf16 __hadd2 accumulation rounding at every
 // step); here accumulation is fp32 in rank order, rounded once, so the result
 // is bit-identical to the other allreduce paths.
-#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -272,9 +271,13 @@ int ce_setup(LzComm* c) {
   return LZE_OK;
 }
 
-// Zero-copy schedule knobs (environment, read per call; defaults are the
-// measured best on 2 x B200):
-//   LZ_CE_CHUNK_MB  chunk size in MiB (default 32);
+// Zero-copy schedule knobs (environment, read per call). Default: two chunks
+// per slice. Every chunk costs a fixed ~20 us (measured on 2 x B200, 1 GiB:
+// 16 chunks 1.729 ms, 8 chunks 1.579 ms, 4 chunks 1.493 ms, 2 chunks
+// 1.450 ms, 1 chunk 1.735 ms without any overlap), so the fewest chunks that
+// still overlap the all-gather of the first chunk with the reduce-scatter of
+// the second win.
+//   LZ_CE_CHUNK_MB  chunk size in MiB (default: slice / 2);
 //   LZ_CE_TAPER     1: the first and last chunks ramp (1/8, 1/4, 1/2 of a
 //                   chunk), shortening the pipeline's fill and drain;
 //   LZ_CE_FLAGS     1: chunk flags go out on their own stream (after an event
@@ -289,8 +292,8 @@ struct CeOpts {
 CeOpts ce_opts() {
   CeOpts o;
   const char* v = getenv("LZ_CE_CHUNK_MB");
-  const long long mb = v ? atoll(v) : 32;
-  o.chunk = (size_t)(mb > 0 ? mb : 32) << 20;
+  const long long mb = v ? atoll(v) : 0;
+  o.chunk = mb > 0 ? (size_t)mb << 20 : 0;  // 0: two chunks per slice
   v = getenv("LZ_CE_TAPER");
   o.taper = v ? atoi(v) : 0;
   v = getenv("LZ_CE_FLAGS");
@@ -312,7 +315,8 @@ int ce_plan(size_t slice, int pipes, const CeOpts& opt, size_t* off, size_t* len
     const size_t cp = (slice / k + 15) / 16 * 16;
     for (size_t o = 0; o < slice && n < kCeMaxChunks; o += cp) sizes[n++] = cp;
   } else {
-    size_t cp = (opt.chunk + 15) / 16 * 16;
+    size_t cp = opt.chunk ? (opt.chunk + 15) / 16 * 16 : ((slice + 1) / 2 + 15) / 16 * 16;
+    if (cp < 16) cp = 16;
     while ((slice + cp - 1) / cp > (size_t)kCeMaxChunks - 6) cp *= 2;
     const size_t ramp[3] = {cp / 8, cp / 4, cp / 2};
     size_t rest = slice;
@@ -346,40 +350,8 @@ int ce_plan(size_t slice, int pipes, const CeOpts& opt, size_t* off, size_t* len
   return m;
 }
 
-// Diagnostic timeline (environment LZ_CE_TRACE=1): timing events after every
-// copy and reduce of one call, printed to stderr (the call synchronises).
-struct CeTrace {
-  bool on = false;
-  int n = 0;
-  cudaEvent_t ev[4 * kCeMaxChunks + 8];
-  char what[4 * kCeMaxChunks + 8][24];
-  void mark(cudaStream_t st, const char* w, int k) {
-    if (!on || n >= (int)(sizeof(ev) / sizeof(ev[0]))) return;
-    cudaEventCreate(&ev[n]);
-    cudaEventRecord(ev[n], st);
-    snprintf(what[n], sizeof(what[n]), "%s %d", w, k);
-    ++n;
-  }
-  void dump(int rank) {
-    if (!on || n == 0) return;
-    cudaEventSynchronize(ev[n - 1]);
-    for (int i = 0; i < n; ++i) {
-      cudaEventSynchronize(ev[i]);
-      float ms = 0.f;
-      cudaEventElapsedTime(&ms, ev[0], ev[i]);
-      fprintf(stderr, "[ce-trace r%d] %8.1f us  %s\n", rank, ms * 1000.f, what[i]);
-      cudaEventDestroy(ev[i]);
-    }
-  }
-};
-
 int ce_twoshot_sym(LzComm* c, const char* in, char* out, size_t bytes, int dtype, int pipes, cudaStream_t s) {
   const int W = c->dev.world, me = c->dev.rank;
-  CeTrace tr;
-  {
-    const char* t = getenv("LZ_CE_TRACE");
-    tr.on = t && atoi(t) != 0;
-  }
   const size_t slice = bytes / W;
   const size_t out_off = lz_comm_heap_offset(c, out, bytes);
   const CeOpts opt = ce_opts();
@@ -407,7 +379,6 @@ int ce_twoshot_sym(LzComm* c, const char* in, char* out, size_t bytes, int dtype
   ce_wait_kernel<<<1, 32, 0, s>>>(c->dev, kCeArStarted, 1, 0, c->ce_seq, peers, 21);
   LZ_CUDA_TRY(cudaGetLastError());
   LZ_CUDA_TRY(cudaEventRecord(ev[kCeEvBegin], s));
-  tr.mark(s, "start", 0);
   // RS: data copies on side stream 0, chunk flags after them (same stream, or
   // the flag stream after a per-chunk event)
   LZ_CUDA_TRY(cudaStreamWaitEvent(rs, ev[kCeEvBegin], 0));
@@ -418,7 +389,6 @@ int ce_twoshot_sym(LzComm* c, const char* in, char* out, size_t bytes, int dtype
       char* dst = c->dev.heap[q] + out_off + (size_t)(me == (q + 1) % W ? q : me) * slice + coffs[k];
       LZ_CUDA_TRY(cudaMemcpyAsync(dst, in + (size_t)q * slice + coffs[k], clens[k], cudaMemcpyDeviceToDevice, rs));
     }
-    tr.mark(rs, "rs-copied", k);
     if (fs != rs) {
       LZ_CUDA_TRY(cudaEventRecord(ev[kCeEvCopied + k], rs));
       LZ_CUDA_TRY(cudaStreamWaitEvent(fs, ev[kCeEvCopied + k], 0));
@@ -454,7 +424,6 @@ int ce_twoshot_sym(LzComm* c, const char* in, char* out, size_t bytes, int dtype
       default: rc = launch_reduce<LZ_BF16>(c, p, G, s);
     }
     if (rc) return rc;
-    tr.mark(s, "reduced", k);
     if (sm_ag) continue;
     LZ_CUDA_TRY(cudaEventRecord(ev[kCeEvRed + k], s));
     LZ_CUDA_TRY(cudaStreamWaitEvent(ag, ev[kCeEvRed + k], 0));
@@ -467,7 +436,6 @@ int ce_twoshot_sym(LzComm* c, const char* in, char* out, size_t bytes, int dtype
       const size_t o = (size_t)me * slice + coffs[k];
       LZ_CUDA_TRY(cudaMemcpyAsync(c->dev.heap[q] + out_off + o, out + o, clens[k], cudaMemcpyDeviceToDevice, ag));
     }
-    tr.mark(ag, "ag-copied", k);
   }
   if (!sm_ag) {
     for (int j = 1; j < W; ++j) {
@@ -483,8 +451,6 @@ int ce_twoshot_sym(LzComm* c, const char* in, char* out, size_t bytes, int dtype
   // every peer's AG into my output has landed
   ce_wait_kernel<<<1, 32, 0, s>>>(c->dev, kCeArDone, 1, 0, c->ce_seq, peers, 23);
   LZ_CUDA_TRY(cudaGetLastError());
-  tr.mark(s, "done", 0);
-  tr.dump(me);
   return LZE_OK;
 }
 

@@ -31,6 +31,7 @@ LABELS = {
     "rhd_sendrecv": "RHD", "twoshot_collective": "2Shot", "twoshot": "P2P", "ring": "RingP2P",
     "compressed_ring": "Comp", "compressed_twoshot": "NoSize", "oneshot": "OneShot", "nvls": "NVLS",
     "nvls_oneshot": "NVLSOneShot", "rhd": "RHDP2P", "compressed": "CompNative",
+    "compressed_hybrid": "CompHybrid",
     "multichannel_ring": "MCRing", "copy_engine": "P2PnoPA", "ll": "LL", "auto": "Auto", "ce": "MemcpyP2P",
 }
 NATIVE = {"oneshot", "twoshot", "nvls", "nvls_oneshot", "ring", "rhd", "ll", "auto", "ce"}
@@ -115,7 +116,7 @@ def main():
     es = torch.empty((), dtype=dtype).element_size()
     variants = a.variants.split(",")
     stage = max(a.max_bytes + 64 * MiB, cz.stage_bytes_needed(a.max_bytes // es, dtype, world) + 64 * MiB) \
-        if "compressed" in variants else a.max_bytes + 64 * MiB
+        if any(v.startswith("compressed") for v in variants) else a.max_bytes + 64 * MiB
     comm = lz.init(config=Config(user_bytes=2 * a.max_bytes + 64 * MiB, stage_bytes=stage,
                                  oneshot_bytes=8 * MiB))
     sizes = []
@@ -154,6 +155,8 @@ def main():
                 fn = lambda v=v: comm.allreduce_(xs, ys, algo=v)
             elif v == "compressed":
                 fn = lambda: cz.compressed_allreduce(xs, ys, comm=comm)
+            elif v == "compressed_hybrid":
+                fn = lambda: cz.compressed_allreduce(xs, ys, comm=comm, hybrid=True)
             elif v in HOST:
                 buf = src.clone()
                 fn = lambda v=v: sendrecv.allreduce(buf, v)
@@ -192,7 +195,7 @@ def main():
             comm.check()
             del graph  # graphs holding NCCL work are released before the group is destroyed
             ok = None
-            if a.check and v in NATIVE | {"compressed"}:
+            if a.check and v in NATIVE | {"compressed", "compressed_hybrid"}:
                 xs.copy_(src)
                 fn()
                 torch.cuda.synchronize()

@@ -59,6 +59,9 @@ def main(argv=None):
     ap.add_argument("--sizes-mb", default="4,64,256,1024")
     ap.add_argument("--sm-budgets", default="16,32,64,0")
     ap.add_argument("--chunks-mb", default="0,64,128,256")
+    ap.add_argument("--variants", default="compressed,hybrid",
+                    help="compressed: reduce-scatter and all-gather compressed; hybrid: raw reduce-scatter, "
+                         "compressed all-gather")
     ap.add_argument("--fp8", action="store_true", default=True)
     ap.add_argument("--no-fp8", dest="fp8", action="store_false")
     ap.add_argument("--iters", type=int, default=5)
@@ -128,15 +131,15 @@ def main(argv=None):
             for b in budgets:
                 st = streams[b]
                 nb = 3 * (st.sm_count if st is not None else sms)
-                for cmb in chunks:
+                for cmb, var in [(cm, vv) for cm in chunks for vv in a.variants.split(",")]:
                     step = (cmb * MiB // 2) if cmb else n
                     if cmb and cmb * MiB >= nbytes:
                         continue
                     parts = [(i, min(step, n - i)) for i in range(0, n, step)]
 
-                    def run():
+                    def run(hybrid=(var == "hybrid")):
                         for i, ln in parts:
-                            cz.compressed_allreduce(x[i:i + ln], y[i:i + ln], comm=comm, nblocks=nb)
+                            cz.compressed_allreduce(x[i:i + ln], y[i:i + ln], comm=comm, nblocks=nb, hybrid=hybrid)
 
                     torch.cuda.reset_peak_memory_stats()
                     m0 = torch.cuda.memory_allocated()
@@ -144,13 +147,13 @@ def main(argv=None):
                     extra = cz.stage_bytes_needed(step, torch.bfloat16, world, nb) + \
                         (torch.cuda.max_memory_allocated() - m0)
                     exact = bool(torch.equal(y, ref))
-                    rows.append({**base, "sm_budget": b or sms, "chunk_mb": cmb, "variant": "compressed",
+                    rows.append({**base, "sm_budget": b or sms, "chunk_mb": cmb, "variant": var,
                                  "ms": round(ms, 4), "algbw_GBps": round(nbytes / ms / 1e6, 2),
                                  "busbw_GBps": round(nbytes / ms / 1e6 * busf, 2), "comp_ratio": round(ratio, 4),
                                  "extra_mem_bytes": int(_max(extra, ctrl)), "exact": exact})
                     if rank == 0:
                         print(f"{kind} {csvfmt.size_label(nbytes):>7} sm={b or sms:3d} chunk={cmb:4d}MB "
-                              f"compressed {ms:8.3f} ms ({nbytes / ms / 1e6 * busf:7.1f} busbw) "
+                              f"{var} {ms:8.3f} ms ({nbytes / ms / 1e6 * busf:7.1f} busbw) "
                               f"nccl {nccl_ms:8.3f} ms ratio {ratio:.3f} "
                               f"exact={exact}", flush=True)
             if a.fp8 and world >= 2:

@@ -22,8 +22,10 @@ MiB = 1 << 20
 # Fitted to CUDA-graph device times of the bf16 sweep on B200
 # (bench/allreduce_sweep.py --graph, max over ranks):
 #   2 GPUs: ll 3.9 us at 1 KB .. 6.2 us at 256 KB (NCCL 14.6 .. 18.4); one-shot
-#           up to 8 MB; two-shot above (NVLS moves (1 + 1/N) S per GPU, which
-#           at N = 2 is more than two-shot's S).
+#           up to 8 MB; two-shot kernel up to 128 MB; copy-engine two-shot
+#           ("ce", symmetric out-of-place buffers) from 256 MB (256 MB: 650 vs
+#           two-shot 592 GB/s busbw; 1 GB: 741 vs 596, NCCL 565). NVLS moves
+#           (1 + 1/N) S per GPU, more than two-shot's S at N = 2.
 #   4 GPUs: ll to 256 KB; one-shot to 2 MB; two-shot 4 MB .. 256 MB; NVLS from
 #           512 MB (1 GB: 2490 us vs NCCL 2523).
 #   8 GPUs: ll to 128 KB; one-shot to 512 KB; two-shot 1 .. 8 MB; NVLS from
@@ -32,7 +34,8 @@ TABLE = {
     2: [
         (256 * 1024, "ll", "ll"),
         (8 * MiB, "oneshot", "oneshot"),
-        (1 << 62, "twoshot", "twoshot"),
+        (128 * MiB, "twoshot", "twoshot"),
+        (1 << 62, "ce", "ce"),
     ],
     4: [
         (256 * 1024, "ll", "ll"),

@@ -16,6 +16,15 @@ def _inputs(world, n, dtype, seed):
     return xs
 
 
+def _ordered(t):
+    """Float bit patterns as integers whose differences count ulps."""
+    if t.element_size() == 2:
+        u = t.view(torch.int16).to(torch.int32)
+        return torch.where(u < 0, -(u & 0x7FFF), u)
+    u = t.view(torch.int32).to(torch.int64)
+    return torch.where(u < 0, -(u & 0x7FFFFFFF), u)
+
+
 def _worker(rank, world, cases):
     import torch
 
@@ -40,7 +49,16 @@ def _worker(rank, world, cases):
 
             res = torch.empty_like(xs[rank])
             for _ in range(3):
-                compressed_allreduce(xs[rank], res, comm=comm, multicast=(algo == "compressed_mc"))
+                compressed_allreduce(xs[rank], res, comm=comm, multicast=algo.endswith("_mc"),
+                                     hybrid="hybrid" in algo)
+        elif algo == "ce_sym":  # zero-copy copy-engine path: symmetric, distinct buffers
+            comm.reset_alloc()
+            xin, res = comm.empty(n, dtype), comm.empty(n, dtype)
+            xin.copy_(xs[rank])
+            for _ in range(3):
+                res.fill_(0)
+                comm.allreduce_(xin, res, algo="ce")
+            res = res.clone()
         elif sym:
             comm.reset_alloc()
             buf = comm.empty(n, dtype)
@@ -54,7 +72,10 @@ def _worker(rank, world, cases):
                 comm.allreduce_(xs[rank], res, algo=algo)
         torch.cuda.synchronize()
         comm.check()
-        if exact:
+        if exact == "ulp1":  # NVLS: fp32 reduction inside the switch, within 1 ulp of the rank-order sum
+            err = int((_ordered(res) - _ordered(ref)).abs().max().item())
+            ok = err <= 1
+        elif exact:
             ok = torch.equal(res, ref)
             err = (res.float() - ref.float()).abs().max().item()
         else:
@@ -74,9 +95,10 @@ CASES = [
     ("ring", "bfloat16", 1 << 20, False, False),
     ("ring", "float32", (1 << 18) + 32, False, False),
     ("rhd", "bfloat16", 1 << 20, False, False),
-    ("nvls", "bfloat16", 1 << 21, True, False),
-    ("nvls", "float32", 1 << 20, False, False),
-    ("nvls", "bfloat16", (1 << 20) + 64, False, False),
+    ("nvls", "bfloat16", 1 << 21, True, "ulp1"),
+    ("nvls", "float32", 1 << 20, False, "ulp1"),
+    ("nvls", "bfloat16", (1 << 20) + 64, False, "ulp1"),
+    ("nvls", "float16", 1 << 20, False, "ulp1"),
     ("nvls_oneshot", "bfloat16", 1 << 14, False, False),
     ("ll", "bfloat16", 1000, False, True),
     ("ll", "float32", 1 << 16, False, True),
@@ -84,6 +106,11 @@ CASES = [
     ("compressed", "bfloat16", (1 << 20) + 48, False, True),
     ("compressed_mc", "bfloat16", 1 << 21, False, True),
     ("compressed", "float32", 300_000, False, True),
+    ("compressed_hybrid", "bfloat16", (1 << 20) + 48, False, True),
+    ("compressed_hybrid_mc", "float16", 1 << 21, False, True),
+    ("ce", "bfloat16", 1 << 20, False, True),
+    ("ce_sym", "bfloat16", (1 << 22) + 64, True, True),
+    ("ce_sym", "float32", 1 << 20, True, True),
 ]
 
 
