@@ -174,24 +174,37 @@ def _input(rank, n, dtype):
     return (torch.randn(n, device="cuda", generator=g) * 1e-2).to(dtype)
 
 
-def _check_full(y, world, n, dtype, ctrl):
-    """Whole-tensor comparison against the fp32 rank-order sum rounded once."""
+def _check_full(ys, world, n, dtype, ctrl):
+    """Whole-tensor comparison of each output in `ys` (name -> tensor) against
+    the fp32 rank-order sum of every rank's input, rounded once."""
     import torch
 
     acc = torch.zeros(n, device="cuda", dtype=torch.float32)
     for r in range(world):
         acc += _input(r, n, dtype).float()
     ref = acc.to(dtype)
-    del acc
-    mism = int((y.view(-1) != ref).sum().item())
-    ulp = int((_ordered_bits(y.view(-1)) - _ordered_bits(ref)).abs().max().item())
-    del ref
+    amax = float(acc.abs().max().item())
+    out = {}
+    for name, y in ys.items():
+        y = y.view(-1)
+        mism = int((y != ref).sum().item())
+        err = float((y.float() - acc).abs().max().item()) / max(amax, 1e-30)
+        ulp = int((_ordered_bits(y) - _ordered_bits(ref)).abs().max().item()) if y.element_size() == 2 else None
+        mism = int(_max_over_ranks(float(mism), ctrl))
+        err = _max_over_ranks(err, ctrl)
+        rec = {"mismatch_elements": mism, "bitexact": mism == 0, "max_abs_err_over_max_abs": err}
+        if ulp is not None:
+            ulp = int(_max_over_ranks(float(ulp), ctrl))
+            rec.update({"max_ulp": ulp, "within_1ulp": ulp <= 1})
+        out[name] = rec
+    del acc, ref
     torch.cuda.empty_cache()
-    mism = int(_max_over_ranks(float(mism), ctrl))
-    ulp = int(_max_over_ranks(float(ulp), ctrl))
-    return {"elements_checked": n, "mismatch_elements": mism, "max_ulp": ulp, "bitexact": mism == 0,
-            "within_1ulp": ulp <= 1,
-            "oracle": "fp32 sum of every rank's input in rank order, rounded once; whole tensor, max over ranks"}
+    res = dict(out.pop("ours", {}))
+    res.update({"elements_checked": n, "oracle": "fp32 sum of every rank's input in rank order, rounded once; "
+                                                 "whole tensor, max over ranks"})
+    if out:
+        res["same_check_of"] = out
+    return res
 
 
 def _e2e(step_fn, host_in, host_out, dev_in, dev_out, steps, warmup, ctrl, local):
@@ -405,18 +418,26 @@ def main():
         comm.check()
     algbw, busbw = bw(ms)
 
-    check = None
-    if args.impl == "ours" and not args.no_check:
-        check = _check_full(y, world, n, dtype, ctrl)
-
     nccl_cmp = None
+    z1 = None
     if args.impl == "ours" and world > 1 and not args.no_nccl_compare:
         z = x.clone()
         n_ms, _ = _timed(lambda: dist.all_reduce(z), args.steps, args.warmup, ctrl, [local])
-        del z
-        torch.cuda.empty_cache()
+        z.copy_(x)
+        dist.all_reduce(z)  # one all_reduce of the same inputs, for the accuracy comparison
+        z1 = z
+        torch.cuda.synchronize()
         nccl_cmp = {"ms": round(n_ms, 4), "busbw_GBps_per_rank": round(bw(n_ms)[1], 3),
                     "ours_over_nccl": round(n_ms / ms, 4)}
+
+    check = None
+    if args.impl == "ours" and not args.no_check:
+        ys = {"ours": y}
+        if z1 is not None:
+            ys["nccl_all_reduce"] = z1
+        check = _check_full(ys, world, n, dtype, ctrl)
+    z1 = None
+    torch.cuda.empty_cache()
 
     e2e = None
     if not args.no_e2e:

@@ -64,24 +64,25 @@ def _max(v, ctrl):
     return float(t.item())
 
 
-def _ulp_distance(y, n, dtype, world) -> int:
-    """Largest ulp distance of the whole output from the fp32 rank-order sum of
-    every rank's input (regenerated from the seeds) rounded once."""
+def _accuracy(y, n, dtype, world):
+    """(largest ulp distance, largest |error| / max |sum|) of the whole output
+    against the fp32 rank-order sum of every rank's input (regenerated from
+    the seeds) rounded once. The ulp distance is given for 16-bit types only:
+    for fp32 outputs near-cancelling sums make it meaningless."""
     acc = torch.zeros(n, device="cuda")
     for r in range(world):
         gg = torch.Generator(device="cuda").manual_seed(100 + r)
         acc += (torch.randn(n, device="cuda", generator=gg) * 1e-2).to(dtype).float()
     ref = acc.to(dtype)
+    rel = float((y[:n].float() - acc).abs().max().item()) / max(float(acc.abs().max().item()), 1e-30)
     del acc
-
-    def ordered(t):
-        if t.element_size() == 2:
-            u = t.view(torch.int16).to(torch.int32)
-            return torch.where(u < 0, -(u & 0x7FFF), u)
-        u = t.view(torch.int32).to(torch.int64)
-        return torch.where(u < 0, -(u & 0x7FFFFFFF), u)
-
-    return int((ordered(y[:n]) - ordered(ref)).abs().max().item())
+    if y.element_size() != 2:
+        return None, rel
+    u = y[:n].view(torch.int16).to(torch.int32)
+    v = ref.view(torch.int16).to(torch.int32)
+    u = torch.where(u < 0, -(u & 0x7FFF), u)
+    v = torch.where(v < 0, -(v & 0x7FFF), v)
+    return int((u - v).abs().max().item()), rel
 
 
 def _capture(fn, fill, iters: int):
@@ -195,11 +196,14 @@ def main():
             comm.check()
             del graph  # graphs holding NCCL work are released before the group is destroyed
             ok = None
-            if a.check and v in NATIVE | {"compressed", "compressed_hybrid"}:
+            if a.check and v in NATIVE | {"compressed", "compressed_hybrid", "nccl"}:
                 xs.copy_(src)
+                if v == "nccl":
+                    buf.copy_(src)
                 fn()
                 torch.cuda.synchronize()
-                ok = _max(float(_ulp_distance(ys, n, dtype, world)), ctrl)
+                ulp, rel = _accuracy(buf if v == "nccl" else ys, n, dtype, world)
+                ok = (None if ulp is None else _max(float(ulp), ctrl), _max(rel, ctrl))
             ratio = None
             if v == "compressed" and rank == 0:
                 ratio = lz.ops.codec.compression_ratio(src) if hasattr(lz, "ops") else None
@@ -221,7 +225,8 @@ def main():
                         "nccl_busbw_GBps": round(nbytes / (bms * 1e-3) / 1e9 * busf, 3) if bms else "",
                         "variant_busbw_GBps": round(algbw * busf, 3),
                         "comp_ratio": round(ratio, 4) if ratio else "",
-                        "max_ulp": "" if ok is None else int(ok),
+                        "max_ulp": "" if ok is None or ok[0] is None else int(ok[0]),
+                        "max_rel_err": "" if ok is None else f"{ok[1]:.3g}",
                     }
                     rows.append(row)
             line = " ".join(f"{LABELS.get(v, v)}={nbytes / (r[0] * 1e-3) / 1e9 * (2 * (world - 1) / world if world > 1 else 1):.1f}"
@@ -231,12 +236,13 @@ def main():
     if rank == 0 and a.csv:
         wall = [r for r in rows if r["metric"] == "wall_ms"]
         cuda = [r for r in rows if r["metric"] == "cuda_ms"]
-        header = csvfmt.SCHEMA_A + (["max_ulp"] if a.check else [])
+        header = csvfmt.SCHEMA_A + (["max_ulp", "max_rel_err"] if a.check else [])
         csvfmt.write_rows(a.csv, header, rows, blocks=[wall, cuda])
         csvfmt.write_sidecar(a.csv, {"bench": "allreduce_sweep", "world": world, "dtype": a.dtype,
                                      "iters": a.iters, "warmup": a.warmup, "include_fill": a.include_fill,
                                      "multicast": comm.has_multicast,
-                                     "graph": a.graph, "check": "max ulp vs fp32 rank-order sum, whole tensor"
+                                     "graph": a.graph, "check": "whole output vs the fp32 rank-order sum rounded once: max ulp (16-bit types) and "
+                                              "max |error| / max |sum|"
                                      if a.check else None,
                                      "timing": "CUDA events per rank, max over ranks" +
                                                ("; timed iterations replayed from one CUDA graph" if a.graph else "")})

@@ -10,6 +10,9 @@ Modes
   ours_direct  native zero-copy raw broadcast into receivers' symmetric weight tensors
                (relay broadcast with multimem.st forwarding for more than 2 ranks)
   ours_ce      copy-engine DMA into each receiver's symmetric weights (no SM moves data)
+  ours_staged  raw broadcast into the receivers' ordinary (non-symmetric) weight tensors:
+               relay broadcast (copy engines at 2 ranks) into double-buffered symmetric
+               staging, copied out on a side stream while the next bucket moves
   nccl_bcast   per-tensor torch.distributed.broadcast, the reference's update path
                (back_up/update_weight_from_distributed.py:422-449)
   nccl_send    per-tensor send from rank 0 to every receiver (batched isend/irecv)
@@ -41,6 +44,7 @@ def parse():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--bucket-mb", type=int, default=1024)
+    ap.add_argument("--stage-mb", type=int, default=256, help="staging buffer size of ours_staged (two of them)")
     ap.add_argument("--encode-fraction", type=float, default=1.0)
     ap.add_argument("--per-tensor", action="store_true")
     ap.add_argument("--per-tensor-iters", type=int, default=20)
@@ -80,6 +84,8 @@ def main():
     total_bytes = shapes.total_params(specs) * 2
     direct = bool({"ours_direct", "ours_ce"} & set(a.modes.split(",")))
     user = (total_bytes + 256 * MiB) if direct else 64 * MiB
+    if "ours_staged" in a.modes.split(","):
+        user += 2 * a.stage_mb * MiB + 64 * MiB
     comm = lz.init(config=Config(user_bytes=user, stage_bytes=512 * MiB, timeout_s=60.0))
     sd = shapes.make_state_dict(specs, seed=1, empty=(rank != 0))
     names = list(sd.keys())
@@ -94,6 +100,9 @@ def main():
     }
 
     def run(mode, ts):
+        if mode == "ours_staged":
+            engines["ours_raw"].broadcast_staged(ts, 0, stage_bytes=a.stage_mb * MiB)
+            return
         if mode == "ours_direct":
             dst = [sym_of[id(t)] for t in ts]
             engines["ours_raw"].broadcast_direct(dst, 0, src_tensors=ts if rank == 0 else None)

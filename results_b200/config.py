@@ -56,6 +56,7 @@ class Config:
     sm_budget: int = 0                # 0: all SMs; otherwise the grid is capped to this
     # algorithm selection (bytes); measured on 8xB200, see results_b200/parallel/tuning.py
     algo: str = "auto"
+    exact: bool = False               # auto picks only bit-exact algorithms (never NVLS)
     # ring / halving-doubling channel knobs of the send/recv reference suite
     ring_channels: int = 4
     hd_max_bytes: int = 128 * MiB
@@ -81,6 +82,7 @@ class Config:
             nthreads=_env_int("LZ_NTHREADS", d.nthreads),
             sm_budget=_env_int("LZ_SM_BUDGET", d.sm_budget),
             algo=_env_str("LZ_ALGO", d.algo),
+            exact=_env_bool("LZ_EXACT", d.exact),
             ring_channels=_env_int("RING_NUM_CHANNELS", _env_int("LZ_RING_CHANNELS", d.ring_channels)),
             hd_max_bytes=_env_int("HD_MAX_MB", d.hd_max_bytes // MiB) * MiB,
             pipeline_min_elements=_env_int("LZ_PIPELINE_MIN_ELEMENTS", d.pipeline_min_elements),

@@ -62,7 +62,8 @@ def select_algo(nbytes: int, world: int, has_multicast: bool, symmetric: bool,
 
     if config is not None and config.algo not in ("", "auto"):
         return ALIASES.get(config.algo, config.algo)
-    return choose(nbytes, world, has_multicast, symmetric, out_of_place)
+    return choose(nbytes, world, has_multicast, symmetric, out_of_place,
+                  exact=bool(config is not None and config.exact))
 
 
 def _padded_allreduce(comm, t: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:

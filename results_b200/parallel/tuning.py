@@ -26,8 +26,13 @@ MiB = 1 << 20
 #           ("ce", symmetric out-of-place buffers) from 256 MB (256 MB: 650 vs
 #           two-shot 592 GB/s busbw; 1 GB: 741 vs 596, NCCL 565). NVLS moves
 #           (1 + 1/N) S per GPU, more than two-shot's S at N = 2.
-#   4 GPUs: ll to 256 KB; one-shot to 2 MB; two-shot 4 MB .. 256 MB; NVLS from
-#           512 MB (1 GB: 2490 us vs NCCL 2523).
+#   4 GPUs: ll to 256 KB; one-shot to 2 MB; two-shot 4 MB .. 256 MB; NVLS at
+#           512 MB (672 vs two-shot 642 GB/s busbw); copy-engine two-shot from
+#           1 GB (689, bit-exact, vs NVLS 685 and NCCL 642).
+# NVLS reduces inside the switch: measured within 1 ulp of the fp32 rank-order
+# sum up to 512 MB and 2-4 ulp at 1 GB (rare near-cancelling elements); with
+# exact=True (Config.exact, LZ_EXACT=1) the table never picks it and the
+# bit-exact copy-engine or two-shot path takes its rows.
 #   8 GPUs: ll to 128 KB; one-shot to 512 KB; two-shot 1 .. 8 MB; NVLS from
 #           16 MB (1 GB: 2329 us vs NCCL 2595, 64 MB: 190 vs 278).
 TABLE = {
@@ -41,7 +46,8 @@ TABLE = {
         (256 * 1024, "ll", "ll"),
         (2 * MiB, "oneshot", "oneshot"),
         (256 * MiB, "twoshot", "twoshot"),
-        (1 << 62, "nvls", "twoshot"),
+        (512 * MiB, "nvls", "twoshot"),
+        (1 << 62, "ce", "ce"),
     ],
     8: [
         (128 * 1024, "ll", "ll"),
@@ -57,14 +63,18 @@ TABLE = {
 }
 
 
-def choose(nbytes: int, world: int, has_multicast: bool, symmetric: bool, out_of_place: bool = True) -> str:
+def choose(nbytes: int, world: int, has_multicast: bool, symmetric: bool, out_of_place: bool = True,
+           exact: bool = False) -> str:
     """Row of TABLE for (world, nbytes). The copy-engine two-shot ("ce") is
     zero-copy only for symmetric, distinct input and output; otherwise the
-    two-shot kernel takes its rows."""
+    two-shot kernel takes its rows. ``exact``: only algorithms whose result is
+    bit-identical to the fp32 rank-order sum (no NVLS)."""
     rows = TABLE.get(world, TABLE["default"])
     for max_b, with_mc, without_mc in rows:
         if nbytes <= max_b:
             algo = with_mc if has_multicast else without_mc
+            if exact and algo.startswith("nvls"):
+                algo = "ce" if nbytes >= 256 * MiB else "twoshot"
             if algo == "ce" and not (symmetric and out_of_place and nbytes % (16 * world) == 0):
                 algo = "twoshot"
             if nbytes % 16 and algo != "oneshot":

@@ -299,6 +299,77 @@ class WeightTransfer:
         _native.check(rc, "direct weight transfer")
         self._keep = descs
 
+    def broadcast_staged(self, dst_tensors, src: int, src_tensors=None, stage_bytes: int = 256 << 20) -> None:
+        """Raw broadcast into ANY destination tensors (not only symmetric ones).
+
+        The bytes go through two symmetric staging buffers of ``stage_bytes``:
+        bucket k is broadcast into buffer k mod 2 with :meth:`broadcast_direct`
+        (relay broadcast with multicast forwarding for more than two ranks,
+        copy engines at two), then every receiver copies it out into its own
+        destination tensors on a side stream while bucket k+1 is broadcast
+        into the other buffer. The broadcast of bucket k+2 waits for the
+        copy-out of bucket k on every rank (stream order before the relay's
+        start barrier). All ranks call with tensors of the same sizes, in the
+        same order; the sender passes its sources as ``src_tensors`` (default:
+        its ``dst_tensors``). Contiguous tensors only.
+        """
+        comm = self.comm
+        if comm.world == 1:
+            if src_tensors is not None:
+                for d, s_ in zip(dst_tensors, src_tensors):
+                    d.copy_(s_)
+            return
+        stage_bytes = max(1 << 20, (stage_bytes + 4095) // 4096 * 4096)
+        st = self.__dict__.get("_stage")
+        if st is None or st[0].numel() < stage_bytes:
+            # collective: every rank allocates the same buffers in the same order
+            st = [comm.empty(stage_bytes, torch.uint8), comm.empty(stage_bytes, torch.uint8)]
+            self._stage = st
+        cap = st[0].numel()
+        me = comm.rank
+        srcs = src_tensors if src_tensors is not None else dst_tensors
+        # pieces: (tensor index, byte offset, bytes) packed into buckets of <= cap
+        buckets, cur, used = [], [], 0
+        for i, d in enumerate(dst_tensors):
+            if not d.is_contiguous() or (me == src and not srcs[i].is_contiguous()):
+                raise ValueError("broadcast_staged needs contiguous tensors")
+            nb = d.numel() * d.element_size()
+            off = 0
+            while off < nb:
+                room = cap - used
+                if room < 4096:
+                    buckets.append(cur)
+                    cur, used = [], 0
+                    room = cap
+                take = min(nb - off, room // 16 * 16)
+                cur.append((i, off, take, used))
+                used = (used + take + 255) // 256 * 256
+                off += take
+        if cur:
+            buckets.append(cur)
+        cs = torch.cuda.current_stream(comm.device)
+        side = self.__dict__.setdefault("_side", torch.cuda.Stream(comm.device))
+        copied = [torch.cuda.Event(), torch.cuda.Event()]
+        sent = torch.cuda.Event()
+        for k, bkt in enumerate(buckets):
+            buf = st[k % 2]
+            if k >= 2:
+                cs.wait_event(copied[k % 2])
+            views = [buf[so:so + n] for (_, _, n, so) in bkt]
+            sviews = None
+            if me == src:
+                sviews = [srcs[i].view(-1).view(torch.uint8)[o:o + n] for (i, o, n, _) in bkt]
+            self.broadcast_direct(views, src, sviews)
+            sent.record(cs)
+            side.wait_event(sent)
+            with torch.cuda.stream(side):
+                for (i, o, n, so), v in zip(bkt, views):
+                    d = dst_tensors[i].view(-1).view(torch.uint8)[o:o + n]
+                    if me != src or d.data_ptr() != srcs[i].view(-1).view(torch.uint8)[o:o + n].data_ptr():
+                        d.copy_(v if me != src else srcs[i].view(-1).view(torch.uint8)[o:o + n])
+                copied[k % 2].record(side)
+        cs.wait_stream(side)
+
     def broadcast(self, tensors, src: int) -> None:
         """All ranks call; `src` sends its tensors, every other rank receives into its own."""
         others = [r for r in range(self.comm.world) if r != src]

@@ -89,21 +89,29 @@ def test_trace_ranges_and_bucket_logs(caplog):
 
 
 def test_size_table_choices():
-    """The measured size table: ll for small messages, one-shot, then two-shot
-    or NVLS by world; unaligned sizes never get a vector-only algorithm."""
+    """The measured size table: ll for small messages, one-shot, then two-shot,
+    NVLS or the copy-engine two-shot by world; the copy-engine path only for
+    symmetric out-of-place buffers; exact mode never picks NVLS; unaligned
+    sizes never get a vector-only algorithm."""
     from results_b200.parallel.tuning import choose
 
     KB, MB = 1 << 10, 1 << 20
     assert choose(1 * KB, 2, True, True) == "ll"
     assert choose(256 * KB, 2, True, True) == "ll"
     assert choose(4 * MB, 2, True, True) == "oneshot"
-    assert choose(1 << 30, 2, True, True) == "twoshot"
+    assert choose(64 * MB, 2, True, True) == "twoshot"
+    assert choose(1 << 30, 2, True, True) == "ce"
+    assert choose(1 << 30, 2, True, True, out_of_place=False) == "twoshot"
+    assert choose(1 << 30, 2, True, False) == "twoshot"
+    assert choose(512 * MB, 4, True, True) == "nvls"
+    assert choose(512 * MB, 4, True, True, exact=True) == "ce"
+    assert choose(64 * MB, 8, True, True, exact=True) == "twoshot"
+    assert choose(1 << 30, 4, True, True) == "ce"
     assert choose(128 * KB, 8, True, True) == "ll"
     assert choose(512 * KB, 8, True, True) == "oneshot"
     assert choose(4 * MB, 8, True, True) == "twoshot"
     assert choose(64 * MB, 8, True, True) == "nvls"
     assert choose(64 * MB, 8, False, True) == "twoshot"
-    assert choose(1 << 30, 4, True, True) == "nvls"
     assert choose(64 * MB, 4, True, True) == "twoshot"
     assert choose(1000 * 2 + 2, 8, True, True) == "oneshot"  # not a multiple of 16 bytes
 

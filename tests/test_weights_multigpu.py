@@ -23,7 +23,7 @@ def _worker(rank, world, cases, dump_dir):
     from results_b200.parallel.comm import Communicator
     from results_b200.parallel import weights
 
-    comm = Communicator(config=Config(user_bytes=64 << 20, stage_bytes=512 << 20, timeout_s=20.0))
+    comm = Communicator(config=Config(user_bytes=96 << 20, stage_bytes=512 << 20, timeout_s=20.0))
     specs = _small_specs()
     ref = make_state_dict(specs, seed=7)
     results = []
@@ -91,6 +91,19 @@ def _worker(rank, world, cases, dump_dir):
     if rank == 1:
         results.append(("raw", "copy_engine", 0.0,
                         all(torch.equal(a.view(torch.int16), b.view(torch.int16)) for a, b in zip(ce, ref.values()))))
+    # staged broadcast into ordinary (non-symmetric) tensors, twice in a row, with
+    # a stage smaller than the largest tensor (pieces, several buckets, both buffers)
+    plain = make_state_dict(specs, empty=True) if rank != 0 else None
+    if rank != 0:
+        for t in plain.values():
+            t.fill_(-9)
+    for _ in range(2):
+        wt.broadcast_staged(list((ref if rank == 0 else plain).values()), 0, stage_bytes=1 << 20)
+    torch.cuda.synchronize()
+    comm.check()
+    if rank != 0:
+        results.append(("raw", "staged", 0.0,
+                        all(torch.equal(plain[k].view(torch.int16), ref[k].view(torch.int16)) for k in ref)))
     # dump oracle: rank 0 dumps, the others compare what they received with it
     if rank == 0:
         weights.dump_tensors(list(ref.items()), dump_dir, 3, 0, group_name="test")
