@@ -155,17 +155,85 @@ bool decode_sub(const uint8_t* stream, uint32_t stream_bytes, const uint32_t* de
   return true;
 }
 
+// PACK symbol section (layout in lz_codec_format.h). Table order: count
+// descending, then symbol ascending.
+uint32_t pack_top(const uint32_t* counts, uint8_t* top_sym, uint32_t* top_cnt) {
+  uint32_t order[256];
+  for (uint32_t s = 0; s < 256; ++s) order[s] = s;
+  std::stable_sort(order, order + 256, [&](uint32_t a, uint32_t b) { return counts[a] > counts[b]; });
+  uint32_t k = 0;
+  for (; k < 15 && counts[order[k]]; ++k) {
+    top_sym[k] = (uint8_t)order[k];
+    top_cnt[k] = counts[order[k]];
+  }
+  return k;
+}
+
+void pack_encode(const uint8_t* syms, uint32_t n, const PackChoice& pc, const uint8_t* top_sym,
+                 uint8_t* symsec) {
+  memset(symsec, 0, pc.bytes);
+  memcpy(symsec, top_sym, pc.nnz);
+  if (pc.bits == 0) return;
+  const uint32_t b = (uint32_t)pc.bits, esc = (1u << b) - 1u;
+  uint8_t code_of[256];
+  memset(code_of, (int)esc, sizeof(code_of));
+  for (uint32_t c = 0; c < pc.nnz; ++c) code_of[top_sym[c]] = (uint8_t)c;
+  uint8_t* codes = symsec + PACK_TABLE_BYTES;
+  uint8_t* escs = codes + pad16(pack_groups(n) * 4u * b);
+  uint32_t e = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    const uint32_t c = code_of[syms[i]];
+    if (c == esc) escs[e++] = syms[i];
+    // code k of group g sits at bit k*b of the group's little-endian words
+    const uint64_t bit = (uint64_t)(i / PACK_GROUP) * 32u * b + (uint64_t)(i % PACK_GROUP) * b;
+    for (uint32_t q = 0; q < b; ++q)
+      if ((c >> q) & 1u) codes[(bit + q) >> 3] |= (uint8_t)(1u << ((bit + q) & 7u));
+  }
+}
+
+// Returns false on a corrupt section.
+bool pack_decode(const uint8_t* symsec, const TgHeader& h, uint32_t n, uint8_t* syms) {
+  const uint32_t b = h.nsub, nnz = h.nnz, nesc = h.reserved;
+  if (b > PACK_MAX_BITS || nnz == 0 || nesc > n) return false;
+  if (b == 0 ? (nnz != 1 || nesc != 0) : nnz > (1u << b) - 1u) return false;
+  if (h.sym_bytes != pack_sym_bytes(n, b, nesc) || h.sym_bytes >= pad16(n)) return false;
+  if (b == 0) {
+    memset(syms, symsec[0], n);
+    return true;
+  }
+  const uint32_t esc = (1u << b) - 1u;
+  const uint8_t* codes = symsec + PACK_TABLE_BYTES;
+  const uint8_t* escs = codes + pad16(pack_groups(n) * 4u * b);
+  uint32_t e = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    const uint64_t bit = (uint64_t)(i / PACK_GROUP) * 32u * b + (uint64_t)(i % PACK_GROUP) * b;
+    uint32_t c = 0;
+    for (uint32_t q = 0; q < b; ++q) c |= (uint32_t)((codes[(bit + q) >> 3] >> ((bit + q) & 7u)) & 1u) << q;
+    if (c == esc) {
+      if (e >= nesc) return false;
+      syms[i] = escs[e++];
+    } else if (c < nnz) {
+      syms[i] = symsec[c];
+    } else {
+      return false;
+    }
+  }
+  return e == nesc;
+}
+
 }  // namespace
 
 extern "C" {
 
-uint32_t lzc_tg_capacity(uint32_t n, int dt) { return tg_capacity_n(n, dt); }
-uint64_t lzc_max_stream_bytes(uint64_t n, int dt) { return max_stream_bytes(n, dt); }
+uint32_t lzc_tg_capacity(uint32_t n, int dt) { return tg_capacity_n(n, codec_dtype(dt)); }
+uint64_t lzc_max_stream_bytes(uint64_t n, int dt) { return max_stream_bytes(n, codec_dtype(dt)); }
 
 // Encodes one TG of n (<= TG_ELEMS) elements into `out` (capacity
-// tg_capacity_n). Returns the record size.
-int64_t lzc_tg_encode(const void* data, uint32_t n, int dt, void* out_) {
-  if (n > TG_ELEMS || !valid_dtype(dt)) return -1;
+// tg_capacity_n). `dt_arg` is the dtype code | level << CODEC_LEVEL_SHIFT.
+// Returns the record size.
+int64_t lzc_tg_encode(const void* data, uint32_t n, int dt_arg, void* out_) {
+  const int dt = codec_dtype(dt_arg), level = codec_level(dt_arg);
+  if (n > TG_ELEMS || !valid_dtype(dt) || !valid_level(level)) return -1;
   uint8_t* out = static_cast<uint8_t*>(out_);
   const uint8_t* in = static_cast<const uint8_t*>(data);
   const int rb = raw_bytes_per_elem(dt);
@@ -187,6 +255,28 @@ int64_t lzc_tg_encode(const void* data, uint32_t n, int dt, void* out_) {
   h.raw_bytes = raw_bytes;
   uint8_t* symsec = raw + raw_bytes;
   const uint32_t raw_sym_bytes = pad16(n);
+  if (level == LEVEL_PACK) {
+    uint8_t top_sym[15];
+    uint32_t top_cnt[15];
+    const uint32_t ntop = pack_top(counts, top_sym, top_cnt);
+    const PackChoice pc = pack_choose(top_cnt, ntop, n);
+    if (pc.bits >= 0) {
+      h.mode = MODE_PACK;
+      h.nnz = (uint16_t)pc.nnz;
+      h.nsub = (uint16_t)pc.bits;
+      h.reserved = pc.nesc;
+      h.sym_bytes = pc.bytes;
+      pack_encode(syms.data(), n, pc, top_sym, symsec);
+    } else {
+      h.mode = MODE_RAW;
+      h.sym_bytes = raw_sym_bytes;
+      memset(symsec, 0, raw_sym_bytes);
+      memcpy(symsec, syms.data(), n);
+    }
+    h.total = (uint32_t)sizeof(TgHeader) + raw_bytes + h.sym_bytes;
+    memcpy(out, &h, sizeof(h));
+    return h.total;
+  }
   bool use_ans = n > 0;
   uint32_t ans_bytes = 0;
   std::vector<uint8_t> ans;
@@ -246,6 +336,7 @@ int64_t lzc_tg_encode(const void* data, uint32_t n, int dt, void* out_) {
 
 // Decodes one TG record. Returns 0, or a negative code on a corrupt record.
 int lzc_tg_decode(const void* rec_, uint64_t rec_cap, void* out, uint32_t n, int dt) {
+  dt = codec_dtype(dt);  // the decoder reads every mode; a level is ignored
   const uint8_t* rec = static_cast<const uint8_t*>(rec_);
   if (rec_cap < sizeof(TgHeader)) return -2;
   TgHeader h;
@@ -288,6 +379,8 @@ int lzc_tg_decode(const void* rec_, uint64_t rec_cap, void* out, uint32_t n, int
         return -11;
       off += pad16(sz);
     }
+  } else if (h.mode == MODE_PACK) {
+    if (!pack_decode(symsec, h, n, syms.data())) return -13;
   } else {
     return -12;
   }
@@ -336,7 +429,10 @@ extern "C" {
 // Whole-tensor compact stream. Returns bytes written or a negative code.
 // Table groups are encoded in parallel into per-TG scratch, then packed in
 // order, so the stream is the same byte for byte whatever the thread count.
-int64_t lzc_encode(const void* data, uint64_t n, int dt, void* out_, uint64_t cap) {
+// `dt_arg`: dtype code | level << CODEC_LEVEL_SHIFT.
+int64_t lzc_encode(const void* data, uint64_t n, int dt_arg, void* out_, uint64_t cap) {
+  const int dt = codec_dtype(dt_arg);
+  if (!valid_dtype(dt) || !valid_level(codec_level(dt_arg))) return -1;
   if (cap < max_stream_bytes(n, dt)) return -1;
   uint8_t* out = static_cast<uint8_t*>(out_);
   const uint64_t ntg = num_tgs(n);
@@ -356,7 +452,7 @@ int64_t lzc_encode(const void* data, uint64_t n, int dt, void* out_, uint64_t ca
   std::vector<int64_t> sizes(ntg, 0);
   parallel_tgs(ntg, [&](uint64_t t) {
     const uint32_t tn = (uint32_t)std::min<uint64_t>(TG_ELEMS, n - t * TG_ELEMS);
-    sizes[t] = lzc_tg_encode(static_cast<const uint8_t*>(data) + t * TG_ELEMS * es, tn, dt, &scratch[t * tcap]);
+    sizes[t] = lzc_tg_encode(static_cast<const uint8_t*>(data) + t * TG_ELEMS * es, tn, dt_arg, &scratch[t * tcap]);
   });
   std::vector<uint64_t> offs(ntg);
   for (uint64_t t = 0; t < ntg; ++t) {
@@ -372,6 +468,7 @@ int64_t lzc_encode(const void* data, uint64_t n, int dt, void* out_, uint64_t ca
 }
 
 int lzc_decode(const void* stream_, uint64_t bytes, void* out, uint64_t n, int dt) {
+  dt = codec_dtype(dt);
   const uint8_t* st = static_cast<const uint8_t*>(stream_);
   if (bytes < sizeof(StreamHeader)) return -2;
   StreamHeader sh;

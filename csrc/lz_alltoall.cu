@@ -59,8 +59,11 @@ LZ_DEV void cta_share_copy(char* __restrict__ dst, const char* __restrict__ src,
   for (; i < v1; i += blockDim.x) st_v4(d + i, ld_cg_v4(s + i));
 }
 
-template <int DT, bool kEnc>
+// KENC: 0 raw bytes, 1 split + rANS records, 2 split + PACK records
+template <int DT, int KENC>
 __device__ __forceinline__ void a2a_body(const LzDevComm& c, const A2aParams& p) {
+  constexpr bool kEnc = KENC != 0;
+  constexpr int kLevel = KENC == 2 ? LEVEL_PACK : LEVEL_ANS;
   extern __shared__ __align__(16) char smem_raw[];
   constexpr int ES = DT == DT_F32 ? 4 : (DT == DT_U8 ? 1 : 2);
   const unsigned long long epoch = epoch_read(c);
@@ -82,7 +85,7 @@ __device__ __forceinline__ void a2a_body(const LzDevComm& c, const A2aParams& p)
       for (uint32_t t = b; t < p.ntg; t += G) {
         const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, p.chunk - (uint64_t)t * TG_ELEMS);
         char* rec = c.heap[dst] + p.slot_off + ((size_t)me * p.ntg + t) * p.cap;
-        if (lz_range_ok(c, rec, p.cap, 23)) encode_tg<DT>(src + (uint64_t)t * TG_ELEMS * ES, tn, rec, sm.enc);
+        if (lz_range_ok(c, rec, p.cap, 23)) encode_tg<DT>(src + (uint64_t)t * TG_ELEMS * ES, tn, rec, sm.enc, kLevel);
       }
     }
   }
@@ -109,31 +112,34 @@ __device__ __forceinline__ void a2a_body(const LzDevComm& c, const A2aParams& p)
   epoch_advance(c);
 }
 
-template <int DT, bool kEnc>
+template <int DT, int KENC>
 __global__ void __launch_bounds__(LZC_THREADS) a2a_kernel(LzDevComm c, A2aParams p) {
-  a2a_body<DT, kEnc>(c, p);
+  a2a_body<DT, KENC>(c, p);
 }
 
 // Single-GPU emulation: block (x, y) is block x of rank y (cooperative launch).
-template <int DT, bool kEnc>
+template <int DT, int KENC>
 __global__ void __launch_bounds__(LZC_THREADS) a2a_emu_kernel(const LzDevComm* cs, const A2aParams* ps) {
-  a2a_body<DT, kEnc>(cs[blockIdx.y], ps[blockIdx.y]);
+  a2a_body<DT, KENC>(cs[blockIdx.y], ps[blockIdx.y]);
 }
 
-void* a2a_fn(int dtype, bool enc, bool emu) {
+// enc: 0 raw, 1 rANS records, 2 PACK records
+void* a2a_fn(int dtype, int enc, bool emu) {
 #define LZ_A2A(D)                                                                            \
-  if (enc) return emu ? reinterpret_cast<void*>(&a2a_emu_kernel<D, true>)                    \
-                      : reinterpret_cast<void*>(&a2a_kernel<D, true>);                       \
-  return emu ? reinterpret_cast<void*>(&a2a_emu_kernel<D, false>)                            \
-             : reinterpret_cast<void*>(&a2a_kernel<D, false>);
+  if (enc == 2) return emu ? reinterpret_cast<void*>(&a2a_emu_kernel<D, 2>)                  \
+                           : reinterpret_cast<void*>(&a2a_kernel<D, 2>);                     \
+  if (enc) return emu ? reinterpret_cast<void*>(&a2a_emu_kernel<D, 1>)                       \
+                      : reinterpret_cast<void*>(&a2a_kernel<D, 1>);                          \
+  return emu ? reinterpret_cast<void*>(&a2a_emu_kernel<D, 0>)                                \
+             : reinterpret_cast<void*>(&a2a_kernel<D, 0>);
   switch (dtype) {
     case LZ_F32: { LZ_A2A(DT_F32) }
     case LZ_F16: { LZ_A2A(DT_F16) }
     case LZ_BF16: { LZ_A2A(DT_BF16) }
     default: {
       if (enc) return nullptr;
-      return emu ? reinterpret_cast<void*>(&a2a_emu_kernel<DT_U8, false>)
-                 : reinterpret_cast<void*>(&a2a_kernel<DT_U8, false>);
+      return emu ? reinterpret_cast<void*>(&a2a_emu_kernel<DT_U8, 0>)
+                 : reinterpret_cast<void*>(&a2a_kernel<DT_U8, 0>);
     }
   }
 #undef LZ_A2A
@@ -216,7 +222,7 @@ extern "C" int lz_all_to_all(LzComm* c, const void* in, void* out, size_t chunk,
     }
   }
   if (G > LZ_MAX_BLOCKS) G = LZ_MAX_BLOCKS;
-  void* fn = a2a_fn(dtype, encode != 0, false);
+  void* fn = a2a_fn(dtype, encode, false);
   const size_t smem = encode ? sizeof(A2aSmem) : 0;
   if (encode) LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* args[] = {&c->dev, &p};
@@ -228,7 +234,7 @@ extern "C" int lz_all_to_all(LzComm* c, const void* in, void* out, size_t chunk,
 extern "C" int lz_emu_all_to_all(LzEmu* e, const void* const* ins, void* const* outs, size_t chunk, int dtype,
                                  int encode, int nblocks, cudaStream_t s) {
   const int R = lz_emu_world(e);
-  void* fn = a2a_fn(dtype, encode != 0, true);
+  void* fn = a2a_fn(dtype, encode, true);
   if (!fn) {
     lz_set_error("emulated all-to-all: unsupported dtype %d", dtype);
     return LZE_ARG;

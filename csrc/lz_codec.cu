@@ -18,7 +18,7 @@ using namespace lzg;
 
 namespace {
 
-template <int DT>
+template <int DT, int LEVEL>
 __global__ void __launch_bounds__(LZC_THREADS, LZC_MIN_BLOCKS) encode_slotted_kernel(const char* __restrict__ in,
                                                                       uint64_t n, char* slots,
                                                                       uint32_t slot_cap,
@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(LZC_THREADS, LZC_MIN_BLOCKS) encode_slotted_ke
   for (uint64_t t = blockIdx.x; t < ntg; t += gridDim.x) {
     const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, n - t * TG_ELEMS);
     const uint32_t bytes =
-        encode_tg<DT>(in + t * (uint64_t)TG_ELEMS * ES, tn, slots + t * (uint64_t)slot_cap, sm, stop_after);
+        encode_tg<DT>(in + t * (uint64_t)TG_ELEMS * ES, tn, slots + t * (uint64_t)slot_cap, sm, LEVEL, stop_after);
     if (threadIdx.x == 0) sizes[t] = bytes;
   }
 }
@@ -182,18 +182,19 @@ int grid_for(uint64_t ntg, int nblocks) {
   }
 
 template <int DT>
-int launch_encode_slotted(const void* in, uint64_t n, void* slots, uint32_t* sizes, int nblocks,
-                          cudaStream_t s) {
+int launch_encode_slotted(const void* in, uint64_t n, void* slots, uint32_t* sizes, int level,
+                          int nblocks, cudaStream_t s) {
   const uint64_t ntg = num_tgs(n);
   if (ntg == 0) return LZE_OK;
   if ((uintptr_t)in % 16 || (uintptr_t)slots % 16) {
     lz_set_error("codec: buffers must be 16-byte aligned");
     return LZE_ARG;
   }
-  int rc = prep_smem(encode_slotted_kernel<DT>, sizeof(EncSmem));
+  auto kernel = level == LEVEL_PACK ? encode_slotted_kernel<DT, LEVEL_PACK> : encode_slotted_kernel<DT, LEVEL_ANS>;
+  int rc = prep_smem(kernel, sizeof(EncSmem));
   if (rc) return rc;
   static const int stop_after = getenv("LZ_CODEC_STOP_AFTER") ? atoi(getenv("LZ_CODEC_STOP_AFTER")) : 0;
-  encode_slotted_kernel<DT><<<grid_for(ntg, nblocks), LZC_THREADS, sizeof(EncSmem), s>>>(
+  kernel<<<grid_for(ntg, nblocks), LZC_THREADS, sizeof(EncSmem), s>>>(
       static_cast<const char*>(in), n, static_cast<char*>(slots), tg_capacity(DT), sizes, stop_after);
   LZ_CUDA_TRY(cudaGetLastError());
   return LZE_OK;
@@ -230,23 +231,31 @@ int launch_decode_stream(const void* st, uint64_t bytes, void* out, uint64_t n, 
 extern "C" {
 
 size_t lz_codec_tg_elems(void) { return TG_ELEMS; }
-size_t lz_codec_tg_capacity(int dtype) { return tg_capacity(dtype); }
-size_t lz_codec_max_bytes(size_t n, int dtype) { return max_stream_bytes(n, dtype); }
+// `dtype` arguments of the entry points below: the dtype code, optionally
+// | level << CODEC_LEVEL_SHIFT (encoders; LEVEL_PACK = fast, lower ratio).
+size_t lz_codec_tg_capacity(int dtype) { return tg_capacity(codec_dtype(dtype)); }
+size_t lz_codec_max_bytes(size_t n, int dtype) { return max_stream_bytes(n, codec_dtype(dtype)); }
 
 // Scratch of the compact encoder: slots + sizes + offsets (+ total).
 size_t lz_codec_scratch_bytes(size_t n, int dtype) {
+  dtype = codec_dtype(dtype);
   const uint64_t ntg = num_tgs(n);
   return ntg * tg_capacity(dtype) + pad16_64(4 * ntg) + pad16_64(8 * ntg) + 16;
 }
 
 int lz_codec_encode_slotted(const void* in, size_t n, int dtype, void* slots, uint32_t* d_sizes,
                             int nblocks, cudaStream_t s) {
-  LZ_DT_DISPATCH(dtype, launch_encode_slotted, in, n, slots, d_sizes, nblocks, s);
+  const int level = codec_level(dtype);
+  if (!valid_level(level)) {
+    lz_set_error("codec: unknown level %d", level);
+    return LZE_ARG;
+  }
+  LZ_DT_DISPATCH(codec_dtype(dtype), launch_encode_slotted, in, n, slots, d_sizes, level, nblocks, s);
 }
 
 int lz_codec_decode_slotted(const void* slots, void* out, size_t n, int dtype, int* d_status,
                             int nblocks, cudaStream_t s) {
-  LZ_DT_DISPATCH(dtype, launch_decode_slotted, slots, out, n, d_status, nblocks, s);
+  LZ_DT_DISPATCH(codec_dtype(dtype), launch_decode_slotted, slots, out, n, d_status, nblocks, s);
 }
 
 // Compact stream: writes the total stream size to *d_total (device memory).
@@ -254,7 +263,8 @@ int lz_codec_encode(const void* in, size_t n, int dtype, void* scratch, size_t s
                     void* out, size_t out_cap, unsigned long long* d_total, int nblocks,
                     cudaStream_t s) {
   const uint64_t ntg = num_tgs(n);
-  if (scratch_bytes < lz_codec_scratch_bytes(n, dtype) || out_cap < max_stream_bytes(n, dtype)) {
+  const int dt = codec_dtype(dtype);
+  if (scratch_bytes < lz_codec_scratch_bytes(n, dt) || out_cap < max_stream_bytes(n, dt)) {
     lz_set_error("codec: scratch (%zu) or output (%zu) too small", scratch_bytes, out_cap);
     return LZE_ARG;
   }
@@ -263,7 +273,7 @@ int lz_codec_encode(const void* in, size_t n, int dtype, void* scratch, size_t s
     return LZE_ARG;
   }
   char* slots = static_cast<char*>(scratch);
-  uint32_t* sizes = reinterpret_cast<uint32_t*>(slots + ntg * tg_capacity(dtype));
+  uint32_t* sizes = reinterpret_cast<uint32_t*>(slots + ntg * tg_capacity(dt));
   uint64_t* offsets = reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(sizes) + pad16_64(4 * ntg));
   int rc = lz_codec_encode_slotted(in, n, dtype, slots, sizes, nblocks, s);
   if (rc) return rc;
@@ -271,7 +281,7 @@ int lz_codec_encode(const void* in, size_t n, int dtype, void* scratch, size_t s
   scan_sizes_kernel<<<1, 1024, 0, s>>>(sizes, ntg, offsets, base, d_total);
   LZ_CUDA_TRY(cudaGetLastError());
   gather_records_kernel<<<grid_for(ntg ? ntg : 1, nblocks), 256, 0, s>>>(
-      slots, tg_capacity(dtype), sizes, offsets, ntg, static_cast<char*>(out), n, dtype, d_total);
+      slots, tg_capacity(dt), sizes, offsets, ntg, static_cast<char*>(out), n, dt, d_total);
   LZ_CUDA_TRY(cudaGetLastError());
   return LZE_OK;
 }
@@ -282,7 +292,7 @@ int lz_codec_decode(const void* stream, size_t stream_bytes, void* out, size_t n
     lz_set_error("codec: buffers must be 16-byte aligned");
     return LZE_ARG;
   }
-  LZ_DT_DISPATCH(dtype, launch_decode_stream, stream, stream_bytes, out, n, d_status, nblocks, s);
+  LZ_DT_DISPATCH(codec_dtype(dtype), launch_decode_stream, stream, stream_bytes, out, n, d_status, nblocks, s);
 }
 
 }  // extern "C"

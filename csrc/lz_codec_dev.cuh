@@ -35,7 +35,17 @@ struct EncSmem {
   uint32_t sub_len[NSUB];
   uint32_t nnz;
   uint32_t total;
+  // PACK level
+  uint8_t codemap[256];  // symbol -> code
+  alignas(16) uint8_t ptab[16];  // code -> symbol (table section), read as one 16-byte vector
+  uint32_t topc[16];     // counts of the table candidates
+  int pk_bits;           // chosen code width, -1 = RAW
+  uint32_t pk_nnz, pk_nesc, pk_bytes;
+  unsigned long long esc_part[NSUB];  // per-warp sums of the escape scan
 };
+
+static_assert(offsetof(EncSmem, ptab) % 16 == 0 && offsetof(EncSmem, syms) % 16 == 0,
+              "vector accesses of the PACK encoder");
 
 struct DecSmem {
   uint32_t dtab[PROB_SCALE];
@@ -46,7 +56,9 @@ struct DecSmem {
   TgHeader h;
   int ok;
   alignas(8) uint64_t bar;  // mbarrier of the bulk copy that stages `sec`
+  unsigned long long esc_part[NSUB];  // per-warp sums of the PACK escape scan
 };
+static_assert(offsetof(DecSmem, syms) % 16 == 0, "vector accesses of the decoders");
 
 LZ_DEV uint32_t lane_id() { return threadIdx.x & 31; }
 LZ_DEV uint32_t lanemask_lt() {
@@ -390,6 +402,332 @@ LZ_DEV bool rans_encode_sub(EncSmem& sm, uint32_t base, uint32_t sn, uint32_t wa
 }
 
 // ---------------------------------------------------------------------------
+// PACK level (layout in lz_codec_format.h): a table of the <= 15 most frequent
+// symbols, b-bit codes in groups of 32 elements, escaped symbols in order.
+// A few integer operations per element on both sides, no serial state.
+// ---------------------------------------------------------------------------
+LZ_DEV void write_tg_header(char* dst, uint8_t mode, uint8_t dt, uint32_t n, uint32_t sym_bytes,
+                            uint32_t raw_bytes, uint32_t nnz, uint32_t nsub, uint32_t reserved) {
+  TgHeader h;
+  h.magic = TG_MAGIC;
+  h.version = VERSION;
+  h.mode = mode;
+  h.dtype = dt;
+  h.n = n;
+  h.sym_bytes = sym_bytes;
+  h.raw_bytes = raw_bytes;
+  h.nnz = (uint16_t)nnz;
+  h.nsub = (uint16_t)nsub;
+  h.total = (uint32_t)sizeof(TgHeader) + raw_bytes + sym_bytes;
+  h.reserved = reserved;
+  const uint4* hv = reinterpret_cast<const uint4*>(&h);
+  st_v4(dst, hv[0]);
+  st_v4(dst + 16, hv[1]);
+}
+
+// Warp 0: the table (count descending, then symbol ascending: the key
+// count << 8 | (255 - sym) orders both at once), the code width, and the
+// symbol -> code map.
+LZ_DEV void pack_tables_warp0(EncSmem& sm, uint32_t n) {
+  const uint32_t lane = lane_id();
+  uint32_t key[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t s = lane * 8 + k, c = sm.hist[s];
+    key[k] = c ? (c << 8) | (255u - s) : 0u;
+  }
+  uint32_t ntop = 0;
+  for (uint32_t r = 0; r < 15; ++r) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m = max(m, key[k]);
+    m = __reduce_max_sync(0xffffffffu, m);
+    if (m == 0) break;  // warp-uniform
+    const uint32_t s = 255u - (m & 0xFFu);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (lane * 8 + k == s) key[k] = 0;
+    if (lane == 0) {
+      sm.ptab[r] = (uint8_t)s;
+      sm.topc[r] = m >> 8;
+    }
+    ntop = r + 1;
+  }
+  __syncwarp();
+  if (lane == 0) {
+    const PackChoice pc = pack_choose(sm.topc, ntop, n);
+    sm.pk_bits = pc.bits;
+    sm.pk_nnz = pc.nnz;
+    sm.pk_nesc = pc.nesc;
+    sm.pk_bytes = pc.bytes;
+  }
+  __syncwarp();
+  const int bits = sm.pk_bits;
+  const uint32_t nnz = sm.pk_nnz;
+  const uint8_t esc = bits > 0 ? (uint8_t)((1u << bits) - 1u) : 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) sm.codemap[lane * 8 + k] = esc;
+  uint8_t t = 0;
+  if (lane < 16) t = lane < nnz ? sm.ptab[lane] : 0;
+  __syncwarp();
+  if (lane < 16) sm.ptab[lane] = t;
+  if (lane < nnz) sm.codemap[t] = (uint8_t)lane;
+}
+
+// Exclusive block scan of per-thread escape counts of up to 4 groups, packed
+// as 16-bit lanes of a u64 (a TG has <= 1024 groups, so a lane sums to at
+// most 8192). *tot receives the block totals (same lanes).
+LZ_DEV unsigned long long esc_scan(unsigned long long v, unsigned long long* part,
+                                   unsigned long long* tot) {
+  const uint32_t lane = lane_id(), warp = threadIdx.x >> 5;
+  unsigned long long incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= (uint32_t)o) incl += t;
+  }
+  if (lane == 31) part[warp] = incl;
+  __syncthreads();
+  unsigned long long before = 0, all = 0;
+  const uint32_t nw = blockDim.x >> 5;
+  for (uint32_t w = 0; w < nw; ++w) {
+    const unsigned long long p = part[w];
+    if (w < warp) before += p;
+    all += p;
+  }
+  *tot = all;
+  return before + incl - v;
+}
+LZ_DEV uint32_t lane16(unsigned long long v, int i) { return (uint32_t)(v >> (16 * i)) & 0xFFFFu; }
+
+// Codes of group g (32 symbols in shared memory) -> w[0..B); returns the
+// escape mask (bit k: element k of the group is escaped).
+template <int B>
+LZ_DEV uint32_t pack_group(const EncSmem& sm, uint32_t g, uint32_t n, uint32_t (&w)[4]) {
+  constexpr uint32_t ESC = (1u << B) - 1u;
+  uint4 sv[2];
+  sv[0] = *reinterpret_cast<const uint4*>(&sm.syms[g * PACK_GROUP]);
+  sv[1] = *reinterpret_cast<const uint4*>(&sm.syms[g * PACK_GROUP + 16]);
+  const uint8_t* sy = reinterpret_cast<const uint8_t*>(sv);
+  const uint32_t lim = n - g * PACK_GROUP;  // >= 1; elements past n take code 0
+#pragma unroll
+  for (int q = 0; q < 4; ++q) w[q] = 0;
+  uint32_t em = 0;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const uint32_t c = (uint32_t)k < lim ? (uint32_t)sm.codemap[sy[k]] : 0u;
+    em |= (c == ESC ? 1u : 0u) << k;
+    const int bit = k * B, wi = bit >> 5, sh = bit & 31;
+    w[wi] |= c << sh;
+    if (sh + B > 32) w[wi + 1] |= c >> (32 - sh);
+  }
+  return em;
+}
+
+template <int B>
+LZ_DEV void pack_emit_codes(EncSmem& sm, uint32_t n, char* symsec) {
+  const uint32_t tid = threadIdx.x;
+  const uint32_t G = pack_groups(n);
+  char* codes = symsec + PACK_TABLE_BYTES;
+  char* escs = codes + pad16(G * 4u * B);
+  uint32_t em[4] = {0, 0, 0, 0};
+  unsigned long long cnt = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t g = tid + (uint32_t)i * blockDim.x;
+    if (g < G) {
+      uint32_t w[4];
+      em[i] = pack_group<B>(sm, g, n, w);
+      char* o = codes + (size_t)g * 4u * B;
+      if (B == 4) {
+        st_v4(o, make_uint4(w[0], w[1], w[2], w[3]));
+      } else if (B == 2) {
+        *reinterpret_cast<uint2*>(o) = make_uint2(w[0], w[1]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < B; ++q) reinterpret_cast<uint32_t*>(o)[q] = w[q];
+      }
+      cnt |= (unsigned long long)__popc(em[i]) << (16 * i);
+    }
+  }
+  // zero padding of the code and escape sections
+  const uint32_t cb = G * 4u * B, cpad = pad16(cb);
+  if (tid < (cpad - cb) / 4) reinterpret_cast<uint32_t*>(codes + cb)[tid] = 0u;
+  const uint32_t nesc = sm.pk_nesc;
+  if (tid < pad16(nesc) - nesc) escs[nesc + tid] = 0;
+  if (nesc == 0) return;  // block-uniform
+  unsigned long long tot;
+  const unsigned long long ex = esc_scan(cnt, sm.esc_part, &tot);
+  uint32_t base = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t g = tid + (uint32_t)i * blockDim.x;
+    uint32_t pos = base + lane16(ex, i);
+    uint32_t m = em[i];
+    while (m) {
+      const int k = __ffs(m) - 1;
+      m &= m - 1;
+      escs[pos++] = (char)sm.syms[g * PACK_GROUP + k];
+    }
+    base += lane16(tot, i);
+  }
+}
+
+// Symbol section and header of a PACK-level record (after the split and the
+// histogram). Returns the record size (uniform over the CTA).
+template <int DT>
+LZ_DEV uint32_t encode_pack_tail(EncSmem& sm, uint32_t n, char* dst, uint32_t raw_bytes) {
+  const uint32_t tid = threadIdx.x;
+  if ((tid >> 5) == 0) pack_tables_warp0(sm, n);
+  __syncthreads();
+  const int bits = sm.pk_bits;
+  char* symsec = dst + sizeof(TgHeader) + raw_bytes;
+  uint32_t sym_bytes;
+  if (bits < 0) {
+    sym_bytes = pad16(n);
+    if (tid < sym_bytes - n) sm.syms[n + tid] = 0;
+    __syncthreads();
+    cta_copy16(symsec, reinterpret_cast<const char*>(sm.syms), sym_bytes);
+    if (tid == 0) write_tg_header(dst, MODE_RAW, (uint8_t)DT, n, sym_bytes, raw_bytes, 0, 0, 0);
+  } else {
+    sym_bytes = sm.pk_bytes;
+    if (tid == 0) st_v4(symsec, *reinterpret_cast<const uint4*>(sm.ptab));
+    switch (bits) {
+      case 1: pack_emit_codes<1>(sm, n, symsec); break;
+      case 2: pack_emit_codes<2>(sm, n, symsec); break;
+      case 3: pack_emit_codes<3>(sm, n, symsec); break;
+      case 4: pack_emit_codes<4>(sm, n, symsec); break;
+      default: break;  // b = 0: the table alone
+    }
+    if (tid == 0)
+      write_tg_header(dst, MODE_PACK, (uint8_t)DT, n, sym_bytes, raw_bytes, sm.pk_nnz, (uint32_t)bits,
+                      sm.pk_nesc);
+  }
+  __syncthreads();  // shared memory is reused by the CTA's next table group
+  return (uint32_t)sizeof(TgHeader) + raw_bytes + sym_bytes;
+}
+
+// Decoder: 4 codes of quad qd of a group as nibbles (code j at bits 4j).
+template <int B>
+LZ_DEV uint32_t quad_codes(const uint32_t (&w)[4], int qd) {
+  const int bit = 4 * B * qd, wi = bit >> 5, sh = bit & 31;
+  uint32_t f = (sh + 4 * B > 32) ? __funnelshift_r(w[wi], w[wi + 1], sh) : (w[wi] >> sh);
+  if (B == 4) return f & 0xFFFFu;
+  uint32_t q = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) q |= ((f >> (j * B)) & ((1u << B) - 1u)) << (4 * j);
+  return q;
+}
+// 4 symbols (one byte each) of the nibble codes q from the 16-byte table.
+template <int B>
+LZ_DEV uint32_t quad_syms(uint32_t q, const uint4& tv) {
+  if (B < 4) return __byte_perm(tv.x, tv.y, q);  // codes <= 7: bit 3 of every nibble is 0
+  const uint32_t sel = q & 0x7777u;
+  const uint32_t lo = __byte_perm(tv.x, tv.y, sel), hi = __byte_perm(tv.z, tv.w, sel);
+  const uint32_t msk = __byte_perm(0x0000FF00u, 0u, (q >> 3) & 0x1111u);  // 0xFF where code >= 8
+  return (lo & ~msk) | (hi & msk);
+}
+// Escape bits (4) of the nibble codes q.
+template <int B>
+LZ_DEV uint32_t quad_esc(uint32_t q) {
+  uint32_t e = q;
+#pragma unroll
+  for (int j = 1; j < B; ++j) e &= q >> j;
+  e &= 0x1111u;
+  return (e | (e >> 3) | (e >> 6) | (e >> 9)) & 0xFu;
+}
+
+template <int B>
+LZ_DEV bool pack_decode_b(const char* __restrict__ symsec, uint32_t n, DecSmem& sm) {
+  constexpr uint32_t ESC = (1u << B) - 1u;
+  const uint32_t tid = threadIdx.x;
+  const uint32_t G = pack_groups(n), nnz = sm.h.nnz, nesc = sm.h.reserved;
+  const uint4 tv = ld_cg_v4(symsec);
+  const char* codes = symsec + PACK_TABLE_BYTES;
+  const char* escs = codes + pad16(G * 4u * B);
+  uint32_t em[4] = {0, 0, 0, 0};
+  unsigned long long cnt = 0;
+  int bad = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t g = tid + (uint32_t)i * blockDim.x;
+    if (g < G) {
+      uint32_t w[4] = {0, 0, 0, 0};
+      const char* o = codes + (size_t)g * 4u * B;
+      if (B == 4) {
+        const uint4 v = ld_cg_v4(o);
+        w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+      } else if (B == 2) {
+        const uint2 v = __ldcg(reinterpret_cast<const uint2*>(o));
+        w[0] = v.x, w[1] = v.y;
+      } else {
+#pragma unroll
+        for (int q = 0; q < B; ++q) w[q] = __ldcg(reinterpret_cast<const uint32_t*>(o) + q);
+      }
+      uint32_t sy[8];
+#pragma unroll
+      for (int qd = 0; qd < 8; ++qd) {
+        const uint32_t q = quad_codes<B>(w, qd);
+        sy[qd] = quad_syms<B>(q, tv);
+        em[i] |= quad_esc<B>(q) << (4 * qd);
+      }
+      const uint32_t lim = n - g * PACK_GROUP;
+      if (lim < PACK_GROUP) em[i] &= (1u << lim) - 1u;
+      if (nnz < ESC) {  // a partial table: codes nnz .. ESC-1 are invalid
+#pragma unroll
+        for (int qd = 0; qd < 8; ++qd) {
+          const uint32_t q = quad_codes<B>(w, qd);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t c = (q >> (4 * j)) & 0xFu;
+            if ((uint32_t)(4 * qd + j) < lim && c >= nnz && c != ESC) bad = 1;
+          }
+        }
+      }
+      uint4* dst = reinterpret_cast<uint4*>(&sm.syms[g * PACK_GROUP]);
+      dst[0] = make_uint4(sy[0], sy[1], sy[2], sy[3]);
+      dst[1] = make_uint4(sy[4], sy[5], sy[6], sy[7]);
+      cnt |= (unsigned long long)__popc(em[i]) << (16 * i);
+    }
+  }
+  if (nesc == 0) return !__syncthreads_or(bad || cnt != 0);  // block-uniform branch
+  unsigned long long tot;
+  const unsigned long long ex = esc_scan(cnt, sm.esc_part, &tot);
+  if (lane16(tot, 0) + lane16(tot, 1) + lane16(tot, 2) + lane16(tot, 3) != nesc) bad = 1;
+  uint32_t base = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t g = tid + (uint32_t)i * blockDim.x;
+    uint32_t pos = base + lane16(ex, i);
+    uint32_t m = em[i];
+    while (m) {
+      const int k = __ffs(m) - 1;
+      m &= m - 1;
+      if (pos < nesc) sm.syms[g * PACK_GROUP + k] = ld_cg_u8(escs + pos);
+      ++pos;
+    }
+    base += lane16(tot, i);
+  }
+  return !__syncthreads_or(bad);
+}
+
+// Symbol plane of a PACK record into sm.syms. Block-uniform result.
+LZ_DEV bool pack_decode_syms(const char* __restrict__ symsec, uint32_t n, DecSmem& sm) {
+  switch (sm.h.nsub) {
+    case 0: {
+      const uint32_t t = (uint32_t)ld_cg_u8(symsec) * 0x01010101u;
+      for (uint32_t o = threadIdx.x * 16; o < pad16(n); o += blockDim.x * 16)
+        *reinterpret_cast<uint4*>(&sm.syms[o]) = make_uint4(t, t, t, t);
+      return true;
+    }
+    case 1: return pack_decode_b<1>(symsec, n, sm);
+    case 2: return pack_decode_b<2>(symsec, n, sm);
+    case 3: return pack_decode_b<3>(symsec, n, sm);
+    default: return pack_decode_b<4>(symsec, n, sm);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Encode one TG of n elements from `in` (16-B aligned) into the record at
 // `dst` (16-B aligned; any memory the CTA can store to: local, peer).
 // Returns the record size (uniform over the CTA).
@@ -398,7 +736,7 @@ LZ_DEV bool rans_encode_sub(EncSmem& sm, uint32_t base, uint32_t sn, uint32_t wa
 // 3 = + rANS, 0 = complete record.
 template <int DT>
 LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restrict__ dst,
-                          EncSmem& sm, int stop_after = 0) {
+                          EncSmem& sm, int level = LEVEL_ANS, int stop_after = 0) {
   using S = Split16<DT>;
   constexpr int RB = DT == DT_F32 ? 3 : (DT == DT_U8 ? 0 : 1);
   constexpr int ES = DT == DT_F32 ? 4 : (DT == DT_U8 ? 1 : 2);
@@ -469,6 +807,7 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
     sm.hist[sbin] = c;
   }
   __syncthreads();
+  if (level == LEVEL_PACK) return encode_pack_tail<DT>(sm, n, dst, raw_bytes);
   if (warp == 0) build_tables_warp0(sm, n);
   __syncthreads();
   if (stop_after == 2) return 0;
@@ -603,6 +942,10 @@ LZ_DEV bool decode_tg_syms(const char* __restrict__ src, uint32_t cap, uint32_t 
              h.raw_bytes == pad16(n * RB) && h.total <= cap &&
              h.total == sizeof(TgHeader) + h.raw_bytes + h.sym_bytes;
     if (ok && h.mode == MODE_RAW) ok = h.sym_bytes == pad16(n);
+    else if (ok && h.mode == MODE_PACK)
+      ok = h.nsub <= PACK_MAX_BITS && h.nnz >= 1 && h.reserved <= n &&
+           (h.nsub == 0 ? (h.nnz == 1 && h.reserved == 0) : h.nnz <= (1u << h.nsub) - 1u) &&
+           h.sym_bytes == pack_sym_bytes(n, h.nsub, h.reserved) && h.sym_bytes < pad16(n);
     else if (ok && h.mode == MODE_ANS)
       ok = h.nsub == (n + SUB_ELEMS - 1) / SUB_ELEMS && h.nnz >= 1 && h.nnz <= 256 &&
            h.sym_bytes < pad16(n) &&
@@ -618,6 +961,8 @@ LZ_DEV bool decode_tg_syms(const char* __restrict__ src, uint32_t cap, uint32_t 
   if (sm.h.mode == MODE_RAW) {
     for (uint32_t o = tid * 16; o < pad16(n); o += blockDim.x * 16)
       *reinterpret_cast<uint4*>(&sm.syms[o]) = ld_cg_v4(symsec + o);
+  } else if (sm.h.mode == MODE_PACK) {
+    if (!pack_decode_syms(symsec, n, sm)) return false;
   } else {
     const uint32_t nnz = sm.h.nnz, nsub = sm.h.nsub;
     // stage the whole ANS section (<= pad16(n) bytes) so every word fetch of

@@ -24,10 +24,26 @@
 //            sizes   nsub x u32 (bytes of each sub-stream before padding), padded to 16 B
 //            nsub sub-streams, each: 32 x u32 final lane states, then the
 //            16-bit words in emission order, padded to 16 B.
-// A TG is coded ANS only if no sub-stream exceeds its sub-block's symbol
-// count in bytes (before padding) and the ANS section is smaller than the RAW
-// section; otherwise it is RAW. Decoding validates the magic, the sizes, that
-// every word was consumed and that every lane state returned to RANS_L.
+//     PACK : table   16 B: the nnz (<= 15) most frequent symbols, most
+//                    frequent first (ties: smaller symbol first), zero padded
+//            codes   one b-bit code per element (b = nsub, 0..4), in groups of
+//                    32 elements: group g is b little-endian u32 words at byte
+//                    4*b*g holding code k of the group at bits [k*b, k*b + b)
+//                    of their 32b-bit concatenation; padded to 16 B
+//            escapes `reserved` symbol bytes, in element order, padded to 16 B
+//            Code c < nnz stands for table[c]; c = 2^b - 1 takes the next
+//            escape byte; other codes are invalid. b = 0 (no code section)
+//            means every element's symbol is table[0].
+// The encoder has two levels. LEVEL_ANS codes a TG ANS only if no sub-stream
+// exceeds its sub-block's symbol count in bytes (before padding) and the ANS
+// section is smaller than the RAW section; otherwise RAW. LEVEL_PACK picks the
+// b in 0..4 with the smallest PACK section (ties: smaller b) and uses it when
+// it is smaller than the RAW section; otherwise RAW. PACK trades ratio (about
+// 3.3 code bits per bf16 exponent of N(0, s) data against ~2.7 for ANS) for
+// an encoder and decoder with a few integer operations per element. Decoding
+// accepts every mode and validates the magic, the sizes, that every word was
+// consumed and every lane state returned to RANS_L (ANS), and the code range
+// and escape count (PACK).
 //
 // Whole-tensor stream ("compact" form):
 //   StreamHeader (64 B) | n_tg x u64 TG offsets (from stream start), padded to 16 B | TG records
@@ -57,6 +73,16 @@ constexpr uint32_t STREAM_MAGIC = 0x31435A4Cu;     // "LZC1"
 constexpr uint16_t VERSION = 1;
 constexpr uint8_t MODE_RAW = 0;
 constexpr uint8_t MODE_ANS = 1;
+constexpr uint8_t MODE_PACK = 2;
+
+// Encoder levels. Host entry points take the level in bits 8..11 of their
+// dtype argument (dtype | level << CODEC_LEVEL_SHIFT); level 0 is ANS.
+constexpr int LEVEL_ANS = 0;
+constexpr int LEVEL_PACK = 1;
+constexpr int CODEC_LEVEL_SHIFT = 8;
+constexpr uint32_t PACK_MAX_BITS = 4;
+constexpr uint32_t PACK_TABLE_BYTES = 16;
+constexpr uint32_t PACK_GROUP = 32;  // elements per code group
 
 // dtype codes (same values as LzDtype). The two fp8 "pair" types treat two
 // consecutive fp8 bytes as one 16-bit element: the pair is packed into a
@@ -95,6 +121,39 @@ static_assert(sizeof(StreamHeader) == 64, "StreamHeader must be 64 bytes");
 
 LZC_HD uint32_t pad16(uint32_t x) { return (x + 15u) & ~15u; }
 LZC_HD uint64_t pad16_64(uint64_t x) { return (x + 15u) & ~uint64_t(15); }
+
+// dtype argument of a host entry point -> dtype code and encoder level
+LZC_HD int codec_dtype(int arg) { return arg & 0xFF; }
+LZC_HD int codec_level(int arg) { return (arg >> CODEC_LEVEL_SHIFT) & 0xF; }
+LZC_HD bool valid_level(int level) { return level == LEVEL_ANS || level == LEVEL_PACK; }
+
+// --- PACK section sizes and the choice of the code width ----------------------
+LZC_HD uint32_t pack_groups(uint32_t n) { return (n + PACK_GROUP - 1) / PACK_GROUP; }
+LZC_HD uint32_t pack_sym_bytes(uint32_t n, uint32_t bits, uint32_t nesc) {
+  return PACK_TABLE_BYTES + pad16(pack_groups(n) * 4u * bits) + pad16(nesc);
+}
+struct PackChoice {
+  int bits;       // -1: PACK does not beat RAW
+  uint32_t nnz;   // table entries
+  uint32_t nesc;  // escaped elements
+  uint32_t bytes; // symbol section bytes
+};
+// top[0..ntop) are the counts of the most frequent symbols in table order
+// (ntop <= 15, all nonzero) of a TG of n elements.
+LZC_HD PackChoice pack_choose(const uint32_t* top, uint32_t ntop, uint32_t n) {
+  PackChoice best{-1, 0, 0, pad16(n)};
+  if (n == 0 || ntop == 0) return best;
+  if (ntop == 1 && top[0] == n && PACK_TABLE_BYTES < best.bytes) best = PackChoice{0, 1, 0, PACK_TABLE_BYTES};
+  uint32_t covered = 0, k = 0;
+  for (uint32_t b = 1; b <= PACK_MAX_BITS; ++b) {
+    const uint32_t K = (1u << b) - 1u;
+    for (; k < K && k < ntop; ++k) covered += top[k];
+    const uint32_t nesc = n - covered;
+    const uint32_t bytes = pack_sym_bytes(n, b, nesc);
+    if (bytes < best.bytes) best = PackChoice{(int)b, k, nesc, bytes};
+  }
+  return best;
+}
 
 LZC_HD int elem_bytes(int dt) { return dt == DT_F32 ? 4 : (dt == DT_U8 ? 1 : 2); }
 LZC_HD bool valid_dtype(int dt) { return dt >= DT_F32 && dt <= DT_E5M2P; }

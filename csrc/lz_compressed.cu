@@ -136,7 +136,7 @@ LZ_DEV void store_rounded(const float* __restrict__ acc, uint32_t n, char* __res
   }
 }
 
-template <int DT>
+template <int DT, int LV>
 __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzParams& p) {
   extern __shared__ __align__(16) char smem_raw[];
   CzSmem& sm = *reinterpret_cast<CzSmem*>(smem_raw);
@@ -172,7 +172,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
       const char* src = p.in + (s0 + (uint64_t)t * TG_ELEMS) * ES;
       char* slot = rs_slot(dst, me, t);
       if (p.hybrid) cta_copy_bytes(slot, src, tn * ES);
-      else encode_tg<DT>(src, tn, slot, sm.enc);
+      else encode_tg<DT>(src, tn, slot, sm.enc, LV);
       publish_block_writes(c);
       if (threadIdx.x == 0) st_release_sys(flag_of(slot), ready);
     }
@@ -207,7 +207,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
       store_rounded<DT>(acc, tn, p.out + e0 * ES);
       __syncthreads();
       char* mine = ag_slot(c.heap[me], me, t);
-      const uint32_t bytes = encode_tg<DT>(p.out + e0 * ES, tn, mine, sm.enc);
+      const uint32_t bytes = encode_tg<DT>(p.out + e0 * ES, tn, mine, sm.enc, LV);
       const uint32_t padded = pad16(bytes);
       if (p.use_mc) {
         char* mc = ag_slot(c.heap_mc, me, t);
@@ -252,32 +252,37 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
   epoch_advance(c);
 }
 
-template <int DT>
+template <int DT, int LV>
 __global__ void __launch_bounds__(LZC_THREADS, LZC_MIN_BLOCKS) cz_allreduce_kernel(LzDevComm c, CzParams p) {
-  cz_allreduce_body<DT>(c, p);
+  cz_allreduce_body<DT, LV>(c, p);
 }
 
 // Single-GPU emulation: block (x, y) is block x of rank y (cooperative launch).
-template <int DT>
+template <int DT, int LV>
 __global__ void __launch_bounds__(LZC_THREADS, LZC_MIN_BLOCKS) cz_allreduce_emu_kernel(const LzDevComm* cs,
                                                                        const CzParams* ps) {
-  cz_allreduce_body<DT>(cs[blockIdx.y], ps[blockIdx.y]);
+  cz_allreduce_body<DT, LV>(cs[blockIdx.y], ps[blockIdx.y]);
 }
 
 template <int DT>
-void* cz_fn(bool emu) {
-  return emu ? reinterpret_cast<void*>(&cz_allreduce_emu_kernel<DT>)
-             : reinterpret_cast<void*>(&cz_allreduce_kernel<DT>);
+void* cz_fn(bool emu, bool pack) {
+  if (pack)
+    return emu ? reinterpret_cast<void*>(&cz_allreduce_emu_kernel<DT, LEVEL_PACK>)
+               : reinterpret_cast<void*>(&cz_allreduce_kernel<DT, LEVEL_PACK>);
+  return emu ? reinterpret_cast<void*>(&cz_allreduce_emu_kernel<DT, LEVEL_ANS>)
+             : reinterpret_cast<void*>(&cz_allreduce_kernel<DT, LEVEL_ANS>);
 }
 
-void* cz_kernel_for(int dtype, bool emu) {
+// flags bit 2: the codec's PACK level instead of rANS
+void* cz_kernel_for(int dtype, bool emu, int flags) {
+  const bool pack = (flags & 4) != 0;
   switch (dtype) {
     case LZ_F32:
-      return cz_fn<DT_F32>(emu);
+      return cz_fn<DT_F32>(emu, pack);
     case LZ_F16:
-      return cz_fn<DT_F16>(emu);
+      return cz_fn<DT_F16>(emu, pack);
     default:
-      return cz_fn<DT_BF16>(emu);
+      return cz_fn<DT_BF16>(emu, pack);
   }
 }
 
@@ -294,7 +299,8 @@ extern "C" size_t lz_cz_stage_bytes(size_t n, int dtype, int world, int nblocks)
 extern "C" int lz_cz_default_blocks(LzComm* c) { return c->sm_count * 3; }
 
 // flags: bit 0 publish the all-gather records with NVLS multimem.st (when a
-// multicast object exists), bit 1 hybrid (raw reduce-scatter).
+// multicast object exists), bit 1 hybrid (raw reduce-scatter), bit 2 PACK
+// codec level (table codes; faster than rANS, lower ratio).
 static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dtype, int G,
                    int flags, CzParams* out_p) {
   const int W = c->dev.world;
@@ -331,7 +337,8 @@ static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dty
 }
 
 // flags: bit 0 multicast all-gather, bit 1 hybrid (raw reduce-scatter, the
-// compressed P2P hybrid of the reference's compressed_p2p_allreduce.py:54-188).
+// compressed P2P hybrid of the reference's compressed_p2p_allreduce.py:54-188),
+// bit 2 PACK codec level.
 extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, size_t n, int dtype,
                                        int nblocks, int flags, cudaStream_t s) {
   const int W = c->dev.world;
@@ -345,7 +352,7 @@ extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, siz
   CzParams p;
   int rc = cz_plan(c, in, out, n, dtype, G, flags, &p);
   if (rc) return rc;
-  void* fn = cz_kernel_for(dtype, false);
+  void* fn = cz_kernel_for(dtype, false, flags);
   const size_t smem = sizeof(CzSmem);
   LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* args[] = {&c->dev, &p};
@@ -357,7 +364,7 @@ extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, siz
 extern "C" int lz_emu_compressed_allreduce(LzEmu* e, const void* const* ins, void* const* outs,
                                            size_t n, int dtype, int nblocks, int flags, cudaStream_t s) {
   const int R = lz_emu_world(e);
-  void* fn = cz_kernel_for(dtype, true);
+  void* fn = cz_kernel_for(dtype, true, flags);
   const size_t smem = sizeof(CzSmem);
   LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;

@@ -46,6 +46,7 @@ int scratch_for_current_device(void** out) {
 }  // namespace
 
 extern "C" size_t lz_codec_noalloc_max_elems(int dtype) {
+  dtype = lzc::codec_dtype(dtype);
   if (!lzc::valid_dtype(dtype)) return 0;
   // largest table-group count whose scratch fits, times the group size
   size_t lo = 0, hi = (size_t)LZ_NOALLOC_SCRATCH_BYTES / 16 + 1;
@@ -60,8 +61,8 @@ extern "C" size_t lz_codec_noalloc_max_elems(int dtype) {
 extern "C" int lz_codec_encode_noalloc(const void* in, size_t n, int dtype, void* out,
                                        size_t out_cap, unsigned long long* d_total,
                                        cudaStream_t stream) {
-  if (!lzc::valid_dtype(dtype)) {
-    lz_set_error("noalloc encoder: unsupported dtype %d", dtype);
+  if (!lzc::valid_dtype(lzc::codec_dtype(dtype)) || !lzc::valid_level(lzc::codec_level(dtype))) {
+    lz_set_error("noalloc encoder: unsupported dtype/level argument %d", dtype);
     return LZE_ARG;
   }
   const size_t need = lz_codec_scratch_bytes(n, dtype);

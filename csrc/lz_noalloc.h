@@ -28,7 +28,8 @@
 //     them on one stream or serialise them.
 //   * Every dtype of lz_codec_encode() is accepted (fp32, fp16, bf16, bytes
 //     and the packed fp8 pair containers e4m3 / e5m2, whose element count is
-//     the number of pairs); output is byte-identical to lz_codec_encode()
+//     the number of pairs), with the encoder level in the same argument
+//     (dtype | level << 8); output is byte-identical to lz_codec_encode()
 //     with caller scratch.
 #pragma once
 #include <stddef.h>

@@ -35,7 +35,7 @@ struct WxDesc {
   char* ptr;        // sender: source bytes; receiver: destination bytes
   uint32_t n;       // elements
   uint8_t dtype;    // LZ dtype code
-  uint8_t encode;   // 1: split+rANS record, 0: raw bytes
+  uint8_t encode;   // 0: raw bytes; 1: split + rANS record; 2: split + PACK record
   uint16_t pad;
 };
 static_assert(sizeof(WxDesc) == 16, "descriptor layout");
@@ -96,24 +96,27 @@ LZ_DEV void push_bytes(const LzDevComm& c, char* dst, const char* src, uint32_t 
 }
 
 template <int DT>
-LZ_DEV uint32_t encode_any(const char* in, uint32_t n, char* dst, EncSmem& sm) {
-  return encode_tg<DT>(in, n, dst, sm);
+LZ_DEV uint32_t encode_any(const char* in, uint32_t n, char* dst, EncSmem& sm, int level) {
+  return level == LEVEL_PACK ? encode_tg<DT>(in, n, dst, sm, LEVEL_PACK)
+                             : encode_tg<DT>(in, n, dst, sm, LEVEL_ANS);
 }
 
-LZ_DEV uint32_t encode_dispatch(int dt, const char* in, uint32_t n, char* dst, EncSmem& sm) {
+// `enc`: descriptor encode field (1 ANS, 2 PACK)
+LZ_DEV uint32_t encode_dispatch(int dt, const char* in, uint32_t n, char* dst, EncSmem& sm, int enc) {
+  const int level = enc == 2 ? LEVEL_PACK : LEVEL_ANS;
   switch (dt) {
     case LZ_F32:
-      return encode_any<DT_F32>(in, n, dst, sm);
+      return encode_any<DT_F32>(in, n, dst, sm, level);
     case LZ_F16:
-      return encode_any<DT_F16>(in, n, dst, sm);
+      return encode_any<DT_F16>(in, n, dst, sm, level);
     case LZ_BF16:
-      return encode_any<DT_BF16>(in, n, dst, sm);
+      return encode_any<DT_BF16>(in, n, dst, sm, level);
     case DT_E4M3P:
-      return encode_any<DT_E4M3P>(in, n, dst, sm);
+      return encode_any<DT_E4M3P>(in, n, dst, sm, level);
     case DT_E5M2P:
-      return encode_any<DT_E5M2P>(in, n, dst, sm);
+      return encode_any<DT_E5M2P>(in, n, dst, sm, level);
     default:
-      return encode_any<DT_U8>(in, n, dst, sm);
+      return encode_any<DT_U8>(in, n, dst, sm, level);
   }
 }
 
@@ -178,7 +181,7 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
           const bool direct = !p.use_mc && nrecv == 1;
           char* dst = direct ? c.heap[only] + slot_off : local;
           if (!lz_range_ok(c, dst, p.cap, 21)) return;
-          const uint32_t bytes = encode_dispatch(d.dtype, d.ptr, d.n, dst, sm.enc);
+          const uint32_t bytes = encode_dispatch(d.dtype, d.ptr, d.n, dst, sm.enc, d.encode);
           if (p.use_mc) {
             push_bytes<true>(c, c.heap_mc + slot_off, local, pad16(bytes));
           } else if (!direct) {

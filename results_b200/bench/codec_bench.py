@@ -52,7 +52,7 @@ def make_data(n, dtype, dist="normal", std=0.02, seed=0):
     return x.to(dtype)
 
 
-def run(sizes_mb, dtype, iters=10, warmup=3, dist="normal", std=0.02, nblocks=0):
+def run(sizes_mb, dtype, iters=10, warmup=3, dist="normal", std=0.02, nblocks=0, level="ans"):
     rows = []
     for mb in sizes_mb:
         nbytes = mb << 20
@@ -72,7 +72,7 @@ def run(sizes_mb, dtype, iters=10, warmup=3, dist="normal", std=0.02, nblocks=0)
         s = torch.cuda.current_stream().cuda_stream
 
         def enc():
-            L.lz_codec_encode(xb.data_ptr(), n, dt, scratch.data_ptr(), scratch.numel(), out.data_ptr(),
+            L.lz_codec_encode(xb.data_ptr(), n, codec.with_level(dt, level), scratch.data_ptr(), scratch.numel(), out.data_ptr(),
                               cap, total.data_ptr(), nblocks, s)
 
         def dcd():
@@ -108,15 +108,18 @@ def main():
     ap.add_argument("--dist", default="normal", choices=["normal", "activation"])
     ap.add_argument("--std", type=float, default=0.02)
     ap.add_argument("--nblocks", type=int, default=0)
+    ap.add_argument("--level", default="ans", choices=sorted(codec.LEVELS))
     ap.add_argument("--csv", default=None)
     a = ap.parse_args()
     dtype = getattr(torch, a.dtype)
-    rows = run([int(s) for s in a.sizes_mb.split(",")], dtype, a.iters, a.warmup, a.dist, a.std, a.nblocks)
+    rows = run([int(s) for s in a.sizes_mb.split(",")], dtype, a.iters, a.warmup, a.dist, a.std, a.nblocks,
+               a.level)
     for r in rows:
         print(r, flush=True)
     if a.csv:
         csvfmt.write_rows(a.csv, csvfmt.SCHEMA_D, rows)
         csvfmt.write_sidecar(a.csv, {"bench": "codec", "dtype": a.dtype, "dist": a.dist, "std": a.std,
+                                     "level": a.level,
                                      "timing": "CUDA events, median of iters"})
 
 

@@ -59,9 +59,10 @@ def main(argv=None):
     ap.add_argument("--sizes-mb", default="4,64,256,1024")
     ap.add_argument("--sm-budgets", default="16,32,64,0")
     ap.add_argument("--chunks-mb", default="0,64,128,256")
-    ap.add_argument("--variants", default="compressed,hybrid",
+    ap.add_argument("--variants", default="compressed,hybrid,compressed_pack,hybrid_pack",
                     help="compressed: reduce-scatter and all-gather compressed; hybrid: raw reduce-scatter, "
-                         "compressed all-gather")
+                         "compressed all-gather; the _pack suffix codes records with the codec's PACK "
+                         "level (table codes) instead of rANS")
     ap.add_argument("--fp8", action="store_true", default=True)
     ap.add_argument("--no-fp8", dest="fp8", action="store_false")
     ap.add_argument("--iters", type=int, default=5)
@@ -113,7 +114,7 @@ def main(argv=None):
         for nbytes in sizes:
             n = nbytes // 2
             x = _data(n, kind, 900 + rank)
-            ratio = _max(codec.compression_ratio(x), ctrl)
+            ratios = {lv: _max(codec.compression_ratio(x, level=lv), ctrl) for lv in ("ans", "pack")}
             acc = torch.zeros(n, device="cuda")
             for r in range(world):  # the exact answer: fp32 sum in rank order, rounded once
                 acc += _data(n, kind, 900 + r).float()
@@ -137,9 +138,13 @@ def main(argv=None):
                         continue
                     parts = [(i, min(step, n - i)) for i in range(0, n, step)]
 
-                    def run(hybrid=(var == "hybrid")):
+                    level = "pack" if var.endswith("_pack") else "ans"
+                    ratio = ratios[level]
+
+                    def run(hybrid=var.startswith("hybrid"), level=level):
                         for i, ln in parts:
-                            cz.compressed_allreduce(x[i:i + ln], y[i:i + ln], comm=comm, nblocks=nb, hybrid=hybrid)
+                            cz.compressed_allreduce(x[i:i + ln], y[i:i + ln], comm=comm, nblocks=nb, hybrid=hybrid,
+                                                    level=level)
 
                     torch.cuda.reset_peak_memory_stats()
                     m0 = torch.cuda.memory_allocated()

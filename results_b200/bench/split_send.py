@@ -6,7 +6,8 @@
 B200 counterpart of the reference's UCCL-P2P benchmark
 (uccl/p2p/benchmarks/benchmark_uccl_collective.py, named at raw/a.txt:590; result
 files raw/result_bf16_split_rank0.csv, csv/p2p_split_send_vs_2baseline.csv):
-sizes 256 B - 1 GB, modes "split" (split+rANS, LZip-P2P split_send), "raw"
+sizes 256 B - 1 GB, modes "split" (split+rANS, LZip-P2P split_send), "pack"
+(split + the codec's PACK level: table codes, faster than rANS), "raw"
 (uncompressed native push) and "nccl" (send/recv baseline). Sweeps of dtype
 (bf16/fp16/fp32/e4m3/e5m2), SM budget (green contexts) and chunking
 (--chunk-mb: the transfer of one size is cut into chunks sent back to back,
@@ -28,8 +29,8 @@ from ..utils import csvfmt
 def parse():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--modes", default="raw,split,nccl",
-                    help="raw, split (split+rANS), nccl, direct (zero copy into a symmetric receive buffer), "
-                         "ce (the same by copy-engine DMA)")
+                    help="raw, split (split+rANS), pack (split + PACK table codes), nccl, direct (zero copy "
+                         "into a symmetric receive buffer), ce (the same by copy-engine DMA)")
     ap.add_argument("--dtype", default="bfloat16")
     ap.add_argument("--min-bytes", type=int, default=256)
     ap.add_argument("--max-bytes", type=int, default=1 << 30)
@@ -66,7 +67,8 @@ def main():
     budget = SmBudget(local, a.sm_budget) if a.sm_budget else None
     nblocks = min(3 * (budget.sm_count if budget else comm.sm_count), 512)
     engines = {"raw": weights.WeightTransfer(comm, mode="raw", nblocks=nblocks),
-               "split": weights.WeightTransfer(comm, mode="split_ans", nblocks=nblocks)}
+               "split": weights.WeightTransfer(comm, mode="split_ans", nblocks=nblocks),
+               "pack": weights.WeightTransfer(comm, mode="split_pack", nblocks=nblocks)}
     rows = []
     size = a.min_bytes
     sizes = []

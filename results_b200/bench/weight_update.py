@@ -6,6 +6,7 @@
 Modes
   ours_raw     native transfer, raw bytes (NVLS multimem broadcast when every rank receives)
   ours_split   native transfer, split+rANS encoded (bit-exact), same paths
+  ours_pack    native transfer, split + the codec's PACK level (table codes), same paths
   ours_p2p     native point-to-point transfer to each receiver in turn (split+rANS)
   ours_direct  native zero-copy raw broadcast into receivers' symmetric weight tensors
                (relay broadcast with multimem.st forwarding for more than 2 ranks)
@@ -96,6 +97,7 @@ def main():
     engines = {
         "ours_raw": weights.WeightTransfer(comm, mode="raw"),
         "ours_split": weights.WeightTransfer(comm, mode="split_ans", encode_fraction=a.encode_fraction),
+        "ours_pack": weights.WeightTransfer(comm, mode="split_pack", encode_fraction=a.encode_fraction),
         "ours_p2p": weights.WeightTransfer(comm, mode="split_ans", encode_fraction=a.encode_fraction),
     }
 
@@ -112,7 +114,7 @@ def main():
             for d in range(1, world):
                 engines["ours_raw"].send_copy_engine(dst, 0, d, src_tensors=ts if rank == 0 else None)
             return
-        if mode in ("ours_raw", "ours_split"):
+        if mode in ("ours_raw", "ours_split", "ours_pack"):
             eng = engines[mode]
             for bkt in weights.buckets(list(zip(range(len(ts)), ts)), bucket):
                 eng.broadcast([t for _, t in bkt], 0)
@@ -209,11 +211,11 @@ def main():
         summary = {"model": a.model, "params": shapes.total_params(specs), "bytes": total_bytes, "world": world,
                    "multicast": comm.has_multicast, "results": results}
         if "nccl_send" in results:
-            for m in ("ours_raw", "ours_split", "ours_direct"):
+            for m in ("ours_raw", "ours_split", "ours_pack", "ours_direct", "ours_ce", "ours_staged"):
                 if m in results:
                     summary[f"speedup_{m}_vs_nccl_send"] = results["nccl_send"]["sec"] / results[m]["sec"]
         if "nccl_bcast" in results:
-            for m in ("ours_raw", "ours_split", "ours_direct"):
+            for m in ("ours_raw", "ours_split", "ours_pack", "ours_direct", "ours_ce", "ours_staged"):
                 if m in results:
                     summary[f"speedup_{m}_vs_nccl_bcast"] = results["nccl_bcast"]["sec"] / results[m]["sec"]
         print(json.dumps(summary), flush=True)

@@ -2,6 +2,7 @@
 
 GPU entry points (sm_100a kernels in csrc/lz_codec.cu):
     blob = encode(t)                      # uint8 CUDA tensor, compact stream
+    blob = encode(t, level="pack")        # fast level: table codes instead of rANS
     t2 = decode(blob, like=t)             # bit-exact reconstruction
     slots, sizes = encode_slotted(t)      # fixed-capacity per-table-group records
 CPU oracle (csrc/cpu/lz_cpu.cpp, bit-identical streams):
@@ -51,6 +52,25 @@ _native_sigs.add_cpu({
 })
 
 TG_ELEMS = 32768
+LEVELS = {"ans": 0, "pack": 1}  # encoder levels (csrc/lz_codec_format.h)
+LEVEL_SHIFT = 8
+
+
+def level_code(level) -> int:
+    """Encoder level name ("ans": rANS, best ratio; "pack": <= 4-bit table
+    codes with escapes, a few integer operations per element) or number."""
+    if isinstance(level, str):
+        if level not in LEVELS:
+            raise ValueError(f"unknown codec level {level!r}; expected one of {sorted(LEVELS)}")
+        return LEVELS[level]
+    if level not in LEVELS.values():
+        raise ValueError(f"unknown codec level {level!r}")
+    return int(level)
+
+
+def with_level(dt: int, level) -> int:
+    """dtype argument of the native encoders: dtype code | level << 8."""
+    return dt | (level_code(level) << LEVEL_SHIFT)
 
 
 class CodecError(RuntimeError):
@@ -99,14 +119,14 @@ def max_encoded_bytes(n: int, dtype: torch.dtype) -> int:
 
 
 # ----------------------------------------------------------------------------- CPU oracle
-def encode_cpu(t: torch.Tensor) -> torch.Tensor:
+def encode_cpu(t: torch.Tensor, level="ans") -> torch.Tensor:
     """Compact LZC1 stream of a contiguous CPU tensor (uint8 tensor)."""
     t = t.detach().contiguous().cpu()
     dt, n = plan(t.dtype, t.numel())
     t = _as_bytes_view(t)
     cap = int(_native.cpu().lzc_max_stream_bytes(n, dt))
     out = torch.empty(cap, dtype=torch.uint8)
-    rc = _native.cpu().lzc_encode(t.data_ptr(), n, dt, out.data_ptr(), cap)
+    rc = _native.cpu().lzc_encode(t.data_ptr(), n, with_level(dt, level), out.data_ptr(), cap)
     if rc < 0:
         raise CodecError(f"lzc_encode failed ({rc})")
     return out[:rc].clone()
@@ -123,12 +143,13 @@ def decode_cpu(blob: torch.Tensor, n: int, dtype: torch.dtype) -> torch.Tensor:
     return out.view(dtype) if store != dtype else out
 
 
-def tg_encode_cpu(t: torch.Tensor) -> torch.Tensor:
+def tg_encode_cpu(t: torch.Tensor, level="ans") -> torch.Tensor:
     """One table-group record (<= 32768 elements)."""
     t = _as_bytes_view(t.detach().contiguous().cpu())
     cap = int(_native.cpu().lzc_tg_capacity(t.numel(), codec_dtype(t.dtype)))
     out = torch.zeros(cap, dtype=torch.uint8)
-    rc = _native.cpu().lzc_tg_encode(t.data_ptr(), t.numel(), codec_dtype(t.dtype), out.data_ptr())
+    rc = _native.cpu().lzc_tg_encode(t.data_ptr(), t.numel(), with_level(codec_dtype(t.dtype), level),
+                                     out.data_ptr())
     if rc < 0:
         raise CodecError(f"lzc_tg_encode failed ({rc})")
     return out[:rc].clone()
@@ -159,15 +180,17 @@ def _stream_ptr(stream=None) -> int:
 
 
 @traced("encode")
-def encode(t: torch.Tensor, nblocks: int = 0, stream=None, return_size: bool = True):
+def encode(t: torch.Tensor, nblocks: int = 0, stream=None, return_size: bool = True, level="ans"):
     """Compress a contiguous CUDA tensor into a compact LZC1 stream.
 
     Returns the stream as a uint8 CUDA tensor trimmed to its size (this reads
     the size back, i.e. synchronises the stream). With ``return_size=False``
     returns ``(buffer, total_bytes_device_tensor)`` without a sync.
+    ``level``: "ans" (rANS symbol sections) or "pack" (table codes, faster,
+    lower ratio); :func:`decode` reads either.
     """
     if not t.is_cuda:
-        return encode_cpu(t)
+        return encode_cpu(t, level)
     L = _native.cuda()
     t = t.contiguous()
     dt, n = plan(t.dtype, t.numel())
@@ -176,7 +199,7 @@ def encode(t: torch.Tensor, nblocks: int = 0, stream=None, return_size: bool = T
     scratch = torch.empty(L.lz_codec_scratch_bytes(n, dt), dtype=torch.uint8, device=t.device)
     out = torch.empty(cap, dtype=torch.uint8, device=t.device)
     total = torch.zeros(1, dtype=torch.int64, device=t.device)
-    _native.check(L.lz_codec_encode(t.data_ptr(), n, dt, scratch.data_ptr(), scratch.numel(),
+    _native.check(L.lz_codec_encode(t.data_ptr(), n, with_level(dt, level), scratch.data_ptr(), scratch.numel(),
                                     out.data_ptr(), cap, total.data_ptr(), nblocks, _stream_ptr(stream)),
                   "lz_codec_encode")
     if not return_size:
@@ -209,7 +232,7 @@ def decode(blob: torch.Tensor, like: torch.Tensor | None = None, n: int | None =
     return res.view(like.shape) if like is not None else res
 
 
-def encode_slotted(t: torch.Tensor, nblocks: int = 0, stream=None):
+def encode_slotted(t: torch.Tensor, nblocks: int = 0, stream=None, level="ans"):
     """Per-table-group records at fixed offsets (t * tg_capacity). Returns (slots, sizes)."""
     L = _native.cuda()
     t = _as_bytes_view(t.contiguous())
@@ -218,7 +241,7 @@ def encode_slotted(t: torch.Tensor, nblocks: int = 0, stream=None):
     cap = L.lz_codec_tg_capacity(dt)
     slots = torch.empty(ntg * cap, dtype=torch.uint8, device=t.device)
     sizes = torch.empty(ntg, dtype=torch.int32, device=t.device)
-    _native.check(L.lz_codec_encode_slotted(t.data_ptr(), n, dt, slots.data_ptr(), sizes.data_ptr(),
+    _native.check(L.lz_codec_encode_slotted(t.data_ptr(), n, with_level(dt, level), slots.data_ptr(), sizes.data_ptr(),
                                             nblocks, _stream_ptr(stream)), "lz_codec_encode_slotted")
     return slots, sizes
 
@@ -238,7 +261,7 @@ def decode_slotted(slots: torch.Tensor, n: int, dtype: torch.dtype, out: torch.T
     return out.view(dtype) if store != dtype else out
 
 
-def compression_ratio(t: torch.Tensor) -> float:
+def compression_ratio(t: torch.Tensor, level="ans") -> float:
     """Measured compressed/raw size of `t` (LZC1 compact stream)."""
-    blob = encode(t) if t.is_cuda else encode_cpu(t)
+    blob = encode(t, level=level) if t.is_cuda else encode_cpu(t, level)
     return blob.numel() / (t.numel() * t.element_size())

@@ -41,16 +41,30 @@ def stage_bytes_needed(numel: int, dtype: torch.dtype, world: int, compress: boo
     return _native.cuda().lz_all_to_all_stage_bytes(numel // world, lz_dtype(dtype), world, int(compress))
 
 
+def enc_code(compress) -> int:
+    """Kernel encode code of the ``compress`` argument: False -> 0 (raw),
+    True or "ans" -> 1 (split + rANS), "pack" -> 2 (split + PACK codes)."""
+    if compress is False or compress is None or compress == 0:
+        return 0
+    if compress is True or compress == "ans" or compress == 1:
+        return 1
+    if compress == "pack":
+        return 2
+    raise ValueError(f"compress must be False, True, 'ans' or 'pack' (got {compress!r})")
+
+
 @traced("all_to_all")
 def all_to_all(x: torch.Tensor, out: torch.Tensor | None = None, compress: bool = False, comm=None,
                nblocks: int = 0, stream=None) -> torch.Tensor:
     """Exchange equal chunks: chunk j of every rank's ``x`` lands as chunk
     ``rank`` of rank j's output. CPU tensors go through ``dist.all_to_all_single``
-    (``compress=True``: LZC1 streams of the CPU codec, sizes exchanged first)."""
+    (``compress=True``: LZC1 streams of the CPU codec, sizes exchanged first).
+    ``compress``: False, True / "ans" (split + rANS records) or "pack"
+    (split + PACK table codes: faster codec, lower ratio)."""
     if not x.is_cuda:
         res = torch.empty_like(x) if out is None else out
-        if compress:
-            return _all_to_all_compressed_cpu(x.contiguous(), res)
+        if enc_code(compress):
+            return _all_to_all_compressed_cpu(x.contiguous(), res, level="pack" if compress == "pack" else "ans")
         dist.all_to_all_single(res, x.contiguous())
         return res
     from .allreduce import get_comm, init
@@ -71,13 +85,13 @@ def all_to_all(x: torch.Tensor, out: torch.Tensor | None = None, compress: bool 
     if dt == 3:
         chunk *= x.element_size()
     s = stream or torch.cuda.current_stream(comm.device)
-    rc = comm._lib.lz_all_to_all(comm.handle, x.data_ptr(), out.data_ptr(), chunk, dt, int(compress),
+    rc = comm._lib.lz_all_to_all(comm.handle, x.data_ptr(), out.data_ptr(), chunk, dt, enc_code(compress),
                                  nblocks, s.cuda_stream)
     _native.check(rc, "all_to_all")
     return out
 
 
-def _all_to_all_compressed_cpu(x: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
+def _all_to_all_compressed_cpu(x: torch.Tensor, out: torch.Tensor, group=None, level="ans") -> torch.Tensor:
     """Host-side compressed all-to-all over any backend: every chunk is
     encoded with the CPU codec, the stream sizes are exchanged, then the
     streams (padded to the largest) and each received stream is decoded into
@@ -90,7 +104,7 @@ def _all_to_all_compressed_cpu(x: torch.Tensor, out: torch.Tensor, group=None) -
     if x.dtype not in COMPRESSIBLE:
         raise ValueError(f"compressed all_to_all supports {COMPRESSIBLE}, got {x.dtype}")
     chunks = x.view(world, -1)
-    blobs = [codec.encode_cpu(chunks[j]) for j in range(world)]
+    blobs = [codec.encode_cpu(chunks[j], level) for j in range(world)]
     sizes = torch.tensor([b.numel() for b in blobs], dtype=torch.int64)
     got_sizes = torch.empty_like(sizes)
     dist.all_to_all_single(got_sizes, sizes, group=group)

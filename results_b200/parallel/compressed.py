@@ -58,8 +58,12 @@ def stage_bytes_needed(n: int, dtype: torch.dtype, world: int, nblocks: int = 44
 @traced("compressed_allreduce")
 def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=None,
                          nblocks: int = 0, multicast: bool = True, stream=None,
-                         hybrid: bool = False) -> torch.Tensor:
+                         hybrid: bool = False, level="ans") -> torch.Tensor:
     """Sum-allreduce with lossless compression on the wire (native fused kernel).
+
+    ``level``: codec level of the records, "ans" (rANS, best ratio) or "pack"
+    (table codes: a few integer operations per element, ratio ~0.70 for bf16
+    instead of ~0.67).
 
     ``hybrid=True`` is the compressed P2P hybrid: the reduce-scatter moves raw
     bytes and only the all-gather of the reduced slices is compressed, so each
@@ -76,7 +80,8 @@ def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=
     s = stream or torch.cuda.current_stream(comm.device)
     nb = nblocks or comm.config.sm_budget
     rc = comm._lib.lz_compressed_allreduce(comm.handle, t.data_ptr(), out.data_ptr(), t.numel(),
-                                           lz_dtype(t.dtype), nb, int(multicast) | (2 if hybrid else 0),
+                                           lz_dtype(t.dtype), nb,
+                                           int(multicast) | (2 if hybrid else 0) | (4 * codec.level_code(level)),
                                            s.cuda_stream)
     _native.check(rc, "compressed_allreduce")
     return out

@@ -62,14 +62,16 @@ class EmulatedWorld:
                                         s.cuda_stream)
         _native.check(rc, f"emulated allreduce[{algo}]")
 
-    def compressed_allreduce(self, ins, outs, nblocks: int = 0, hybrid: bool = False):
+    def compressed_allreduce(self, ins, outs, nblocks: int = 0, hybrid: bool = False, level="ans"):
         from . import compressed  # noqa: F401  (declares the native signature)
+        from ..ops import codec
 
         R = self.world
         arr_in = (C.c_void_p * R)(*[t.data_ptr() for t in ins])
         arr_out = (C.c_void_p * R)(*[t.data_ptr() for t in outs])
         rc = self._lib.lz_emu_compressed_allreduce(self._emu, arr_in, arr_out, ins[0].numel(),
-                                                   lz_dtype(ins[0].dtype), nblocks, 2 if hybrid else 0,
+                                                   lz_dtype(ins[0].dtype), nblocks,
+                                                   (2 if hybrid else 0) | 4 * codec.level_code(level),
                                                    torch.cuda.current_stream().cuda_stream)
         _native.check(rc, "emulated compressed allreduce")
 
@@ -122,7 +124,9 @@ class EmulatedWorld:
         chunk = x.numel() // R * (1 if dt != 3 else x.element_size())
         arr_in = (C.c_void_p * R)(*[t.data_ptr() for t in ins])
         arr_out = (C.c_void_p * R)(*[t.data_ptr() for t in outs])
-        rc = self._lib.lz_emu_all_to_all(self._emu, arr_in, arr_out, chunk, dt, int(compress), nblocks,
+        from .alltoall import enc_code
+
+        rc = self._lib.lz_emu_all_to_all(self._emu, arr_in, arr_out, chunk, dt, enc_code(compress), nblocks,
                                          torch.cuda.current_stream().cuda_stream)
         _native.check(rc, "emulated all_to_all")
 

@@ -53,7 +53,9 @@ _native_sigs.add_cuda({
 })
 
 TG = 32768
-MODES = ("raw", "split_ans")
+MODES = ("raw", "split_ans", "split_pack")
+# descriptor encode field per mode: 0 raw, 1 split + rANS, 2 split + PACK codes
+_ENCODE_CODE = {"raw": 0, "split_ans": 1, "split_pack": 2}
 
 
 def _encode_flags(n_tensors: int, fraction: float):
@@ -62,7 +64,8 @@ def _encode_flags(n_tensors: int, fraction: float):
 
 
 def build_descriptors(tensors, encode, device) -> tuple[torch.Tensor, int]:
-    """16-byte descriptor per table group: (ptr, n | dtype << 32 | encode << 40)."""
+    """16-byte descriptor per table group: (ptr, n | dtype << 32 | encode << 40),
+    encode = 0 (raw), 1 (split + rANS, also for True) or 2 (split + PACK codes)."""
     rows_ptr, rows_meta = [], []
     for t, enc in zip(tensors, encode):
         if not t.is_contiguous():
@@ -79,7 +82,10 @@ def build_descriptors(tensors, encode, device) -> tuple[torch.Tensor, int]:
         idx = torch.arange(ntg, dtype=torch.int64)
         rows_ptr.append(base + idx * (TG * es))
         n = torch.clamp(numel - idx * TG, max=TG)
-        rows_meta.append(n | (dt << 32) | (int(bool(enc)) << 40))
+        code = int(enc)
+        if code not in (0, 1, 2):
+            raise ValueError(f"encode code {enc!r} must be 0, 1 or 2")
+        rows_meta.append(n | (dt << 32) | (code << 40))
     if not rows_ptr:
         return torch.empty(0, dtype=torch.int64, device=device), 0
     d = torch.stack([torch.cat(rows_ptr), torch.cat(rows_meta)], dim=1).contiguous()
@@ -95,7 +101,7 @@ class WeightTransfer:
             raise ValueError(f"mode must be one of {MODES}")
         self.comm = comm
         self.mode = mode
-        self.encode_fraction = encode_fraction if mode == "split_ans" else 0.0
+        self.encode_fraction = encode_fraction if mode != "raw" else 0.0
         self.nblocks = nblocks or comm.sm_count * 2
         cap_tg_bytes = TG * 2
         if kslots:
@@ -134,7 +140,8 @@ class WeightTransfer:
 
     def _flags(self, tensors):
         f = self.encode_fraction
-        return _encode_flags(len(tensors), f) if f > 0 else [False] * len(tensors)
+        code = _ENCODE_CODE[self.mode]
+        return [code if e else 0 for e in _encode_flags(len(tensors), f)] if f > 0 else [0] * len(tensors)
 
     def send(self, tensors, dsts, broadcast_all: bool = False) -> None:
         tensors = list(tensors.values()) if isinstance(tensors, dict) else list(tensors)
@@ -400,7 +407,7 @@ def buckets(named, max_bytes: int):
 class HostTransfer:
     """Weight transfer of CPU tensors over any torch.distributed backend
     (gloo): per tensor, raw bytes, or an LZC1 stream of the CPU codec with its
-    size sent first (``split_ans``). The same public calls (send / recv /
+    size sent first (``split_ans`` / ``split_pack``). The same public calls (send / recv /
     broadcast) as :class:`WeightTransfer`; receivers end bit-identical."""
 
     def __init__(self, mode: str = "split_ans", group=None):
@@ -409,7 +416,9 @@ class HostTransfer:
         self.mode, self.group = mode, group
 
     def _encode(self, t):
-        return codec.encode_cpu(t) if self.mode == "split_ans" and t.dtype in _CODEC_DTYPES else None
+        if self.mode == "raw" or t.dtype not in _CODEC_DTYPES:
+            return None
+        return codec.encode_cpu(t, level="pack" if self.mode == "split_pack" else "ans")
 
     def send(self, tensors, dsts) -> None:
         dsts = [dsts] if isinstance(dsts, int) else list(dsts)
@@ -424,7 +433,7 @@ class HostTransfer:
 
     def recv(self, tensors, src: int) -> None:
         for t in tensors:
-            if self.mode != "split_ans" or t.dtype not in _CODEC_DTYPES:
+            if self.mode == "raw" or t.dtype not in _CODEC_DTYPES:
                 buf = t if t.is_contiguous() else torch.empty_like(t)
                 dist.recv(buf, src, group=self.group)
                 if buf is not t:

@@ -1,4 +1,4 @@
-"""All-to-all kernel (raw zero-copy, raw via slots, split+rANS compressed)
+"""All-to-all kernel (raw zero-copy, raw via slots, split+rANS or split+PACK compressed)
 with R ranks emulated on ONE GPU in one cooperative launch; every output
 chunk must equal the matching input chunk of its source rank bit for bit."""
 import pytest
@@ -13,7 +13,7 @@ def _expect(ins, R):
 
 
 @pytest.mark.parametrize("R", [2, 4, 8])
-@pytest.mark.parametrize("mode", ["raw_slots", "raw_symmetric", "compressed"])
+@pytest.mark.parametrize("mode", ["raw_slots", "raw_symmetric", "compressed", "compressed_pack"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_emulated_all_to_all(R, mode, dtype):
     from results_b200.parallel.emulate import EmulatedWorld
@@ -29,7 +29,8 @@ def test_emulated_all_to_all(R, mode, dtype):
                 outs = w.empty(n, dtype)
             else:
                 outs = [torch.full((n,), 7.0, device="cuda", dtype=dtype) for _ in range(R)]
-            w.all_to_all(ins, outs, compress=(mode == "compressed"), nblocks=4)
+            comp = {"compressed": True, "compressed_pack": "pack"}.get(mode, False)
+            w.all_to_all(ins, outs, compress=comp, nblocks=4)
             torch.cuda.synchronize()
             for r, ref in enumerate(_expect(ins, R)):
                 assert w.status(r) == 0

@@ -30,17 +30,19 @@ def _inputs(R, n, dtype, seed, kind="grad"):
     return xs
 
 
+@pytest.mark.parametrize("level", ["ans", "pack"])
 @pytest.mark.parametrize("hybrid", [False, True])
 @pytest.mark.parametrize("R", [2, 4])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("n", [16, 1000, 32768 * 3 + 48, 400_000, 400_001])
-def test_compressed_allreduce_bitexact(worlds, R, dtype, n, hybrid):
-    """hybrid=True: raw reduce-scatter, compressed all-gather."""
+def test_compressed_allreduce_bitexact(worlds, R, dtype, n, hybrid, level):
+    """hybrid=True: raw reduce-scatter, compressed all-gather; level: codec
+    level of the records (rANS or PACK table codes)."""
     w = worlds[R]
     xs = _inputs(R, n, dtype, seed=n + R)
     outs = [torch.empty_like(x) for x in xs]
     for _ in range(2):
-        w.compressed_allreduce(xs, outs, nblocks=8, hybrid=hybrid)
+        w.compressed_allreduce(xs, outs, nblocks=8, hybrid=hybrid, level=level)
     torch.cuda.synchronize()
     acc = xs[0].float().clone()
     for x in xs[1:]:
@@ -51,7 +53,8 @@ def test_compressed_allreduce_bitexact(worlds, R, dtype, n, hybrid):
         assert torch.equal(outs[r].view(torch.uint8), ref.view(torch.uint8)), f"rank {r}"
 
 
-def test_compressed_inplace_activation_like(worlds):
+@pytest.mark.parametrize("level", ["ans", "pack"])
+def test_compressed_inplace_activation_like(worlds, level):
     R = 4
     w = worlds[R]
     n = 300_000
@@ -59,7 +62,7 @@ def test_compressed_inplace_activation_like(worlds):
     xs = _inputs(R, n, torch.bfloat16, seed=5, kind="act")
     for r in range(R):
         bufs[r].copy_(xs[r])
-    w.compressed_allreduce(bufs, bufs, nblocks=16)
+    w.compressed_allreduce(bufs, bufs, nblocks=16, level=level)
     torch.cuda.synchronize()
     acc = xs[0].float().clone()
     for x in xs[1:]:

@@ -26,12 +26,12 @@ def _tensors(seed, device="cuda"):
     return out
 
 
-@pytest.mark.parametrize("encode", [True, False])
+@pytest.mark.parametrize("encode", [1, 0, 2])  # split + rANS, raw, split + PACK codes
 @pytest.mark.parametrize("bcast", [False, True])
 def test_emulated_transfer_repeated(world3, encode, bcast):
     R = 3
     for it in range(4):
-        src_t = _tensors(100 * it + int(encode) + 2 * int(bcast))
+        src_t = _tensors(100 * it + int(encode) + 3 * int(bcast))
         recv = {r: [torch.full_like(t, 0) for t in src_t] for r in (1, 2)}
         tensors = [src_t, recv[1], recv[2]]
         if bcast:
