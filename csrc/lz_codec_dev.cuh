@@ -648,22 +648,32 @@ LZ_DEV bool pack_decode_b(const char* __restrict__ symsec, uint32_t n, DecSmem& 
   uint32_t em[4] = {0, 0, 0, 0};
   unsigned long long cnt = 0;
   int bad = 0;
+  // all code loads of the thread's (<= 4) groups are issued before any is used
+  uint32_t wv[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t g = tid + (uint32_t)i * blockDim.x;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) wv[i][q] = 0;
+    if (g < G) {
+      const char* o = codes + (size_t)g * 4u * B;
+      if (B == 4) {
+        const uint4 v = ld_cg_v4(o);
+        wv[i][0] = v.x, wv[i][1] = v.y, wv[i][2] = v.z, wv[i][3] = v.w;
+      } else if (B == 2) {
+        const uint2 v = __ldcg(reinterpret_cast<const uint2*>(o));
+        wv[i][0] = v.x, wv[i][1] = v.y;
+      } else {
+#pragma unroll
+        for (int q = 0; q < B; ++q) wv[i][q] = __ldcg(reinterpret_cast<const uint32_t*>(o) + q);
+      }
+    }
+  }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t g = tid + (uint32_t)i * blockDim.x;
     if (g < G) {
-      uint32_t w[4] = {0, 0, 0, 0};
-      const char* o = codes + (size_t)g * 4u * B;
-      if (B == 4) {
-        const uint4 v = ld_cg_v4(o);
-        w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
-      } else if (B == 2) {
-        const uint2 v = __ldcg(reinterpret_cast<const uint2*>(o));
-        w[0] = v.x, w[1] = v.y;
-      } else {
-#pragma unroll
-        for (int q = 0; q < B; ++q) w[q] = __ldcg(reinterpret_cast<const uint32_t*>(o) + q);
-      }
+      const uint32_t(&w)[4] = wv[i];
       uint32_t sy[8];
 #pragma unroll
       for (int qd = 0; qd < 8; ++qd) {
@@ -1087,12 +1097,32 @@ LZ_DEV void merge_store(const char* __restrict__ raw, const DecSmem& sm, uint32_
   using S = Split16<DT>;
   constexpr int RB = DT == DT_F32 ? 3 : (DT == DT_U8 ? 0 : 1);
   constexpr int ES = DT == DT_F32 ? 4 : (DT == DT_U8 ? 1 : 2);
-  const uint32_t tid = threadIdx.x;
+  constexpr int RV = S::RAW_BYTES / 16;            // raw vectors per unit
+  constexpr int NB = S::RAW_BYTES > 16 ? 2 : 4;     // units whose raw loads are in flight together
+  const uint32_t tid = threadIdx.x, bd = blockDim.x;
   const uint32_t units = n / 16;
-  for (uint32_t u = tid; u < units; u += blockDim.x) {
-    alignas(16) uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 16];
+  uint32_t u = tid;
+  for (; u + (NB - 1) * bd < units; u += NB * bd) {
+    alignas(16) uint8_t rw[NB][RV > 0 ? S::RAW_BYTES : 16];
 #pragma unroll
-    for (int q = 0; q < S::RAW_BYTES / 16; ++q)
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int q = 0; q < RV; ++q)
+        reinterpret_cast<uint4*>(rw[b])[q] = ld_cg_v4(raw + (size_t)(u + b * bd) * S::RAW_BYTES + 16 * q);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      const uint32_t ub = u + b * bd;
+      uint4 sv = *reinterpret_cast<const uint4*>(&sm.syms[ub * 16]);
+      uint4 v[S::IN_VECS];
+      S::merge(reinterpret_cast<const uint8_t*>(&sv), rw[b], v);
+#pragma unroll
+      for (int q = 0; q < S::IN_VECS; ++q) st_v4(out + (size_t)ub * 16 * ES + 16 * q, v[q]);
+    }
+  }
+  for (; u < units; u += bd) {
+    alignas(16) uint8_t rw[RV > 0 ? S::RAW_BYTES : 16];
+#pragma unroll
+    for (int q = 0; q < RV; ++q)
       reinterpret_cast<uint4*>(rw)[q] = ld_cg_v4(raw + (size_t)u * S::RAW_BYTES + 16 * q);
     uint4 sv = *reinterpret_cast<const uint4*>(&sm.syms[u * 16]);
     uint4 v[S::IN_VECS];
@@ -1116,50 +1146,6 @@ LZ_DEV float elem_to_f32(uint8_t sym, const uint8_t* raw) {
   if (DT == DT_F16) return __half2float(__ushort_as_half(merge_f16(sym, raw[0])));
   const uint32_t r = raw[0] | ((uint32_t)raw[1] << 8) | ((uint32_t)raw[2] << 16);
   return __uint_as_float(merge_f32(sym, r));
-}
-
-// acc[i] (fp32, global scratch) = or += value of element i. Same thread owns
-// the same 16 elements in every call, so no synchronisation between calls.
-template <int DT>
-LZ_DEV void merge_accumulate(const char* __restrict__ raw, const DecSmem& sm, uint32_t n,
-                             float* __restrict__ acc, bool first) {
-  using S = Split16<DT>;
-  constexpr int RB = DT == DT_F32 ? 3 : 1;
-  const uint32_t tid = threadIdx.x;
-  const uint32_t units = (n + 15) / 16;
-  for (uint32_t u = tid; u < units; u += blockDim.x) {
-    alignas(16) uint8_t rw[S::RAW_BYTES];
-    uint8_t sy[16];
-    if ((u + 1) * 16 <= n) {
-#pragma unroll
-      for (int q = 0; q < S::RAW_BYTES / 16; ++q)
-        reinterpret_cast<uint4*>(rw)[q] = ld_cg_v4(raw + (size_t)u * S::RAW_BYTES + 16 * q);
-      *reinterpret_cast<uint4*>(sy) = *reinterpret_cast<const uint4*>(&sm.syms[u * 16]);
-    } else {
-      for (int k = 0; k < 16; ++k) {
-        const uint32_t i = u * 16 + k;
-        sy[k] = i < n ? sm.syms[i] : 0;
-        for (int q = 0; q < RB; ++q) rw[k * RB + q] = i < n ? ld_cg_u8(raw + (size_t)i * RB + q) : 0;
-      }
-    }
-    float4* a4 = reinterpret_cast<float4*>(acc + (size_t)u * 16);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float4 v;
-      v.x = elem_to_f32<DT>(sy[4 * q + 0], rw + (4 * q + 0) * RB);
-      v.y = elem_to_f32<DT>(sy[4 * q + 1], rw + (4 * q + 1) * RB);
-      v.z = elem_to_f32<DT>(sy[4 * q + 2], rw + (4 * q + 2) * RB);
-      v.w = elem_to_f32<DT>(sy[4 * q + 3], rw + (4 * q + 3) * RB);
-      if (!first) {
-        const float4 o = a4[q];
-        v.x = o.x + v.x;
-        v.y = o.y + v.y;
-        v.z = o.z + v.z;
-        v.w = o.w + v.w;
-      }
-      a4[q] = v;
-    }
-  }
 }
 
 // Decode one TG record at `src` (n elements expected) into `out`.

@@ -70,54 +70,6 @@ LZ_DEV uint64_t slice_len(const CzParams& p, int s) {
 }
 LZ_DEV uint32_t ntg_of(const CzParams& p, int s) { return (uint32_t)num_tgs(slice_len(p, s)); }
 
-template <int DT>
-LZ_DEV void accumulate_plain(const char* __restrict__ in, uint32_t n, float* __restrict__ acc,
-                             bool first) {
-  constexpr int ES = DT == DT_F32 ? 4 : 2;
-  for (uint32_t i0 = threadIdx.x * 16; i0 < n; i0 += blockDim.x * 16) {
-    float v[16];
-    if (i0 + 16 <= n) {
-      uint4 raw[ES * 16 / 16];
-#pragma unroll
-      for (int q = 0; q < ES; ++q) raw[q] = ld_cg_v4(in + (size_t)i0 * ES + 16 * q);
-      if (DT == DT_F32) {
-        const float* f = reinterpret_cast<const float*>(raw);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] = f[k];
-      } else if (DT == DT_BF16) {
-        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(raw);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] = __bfloat162float(h[k]);
-      } else {
-        const __half* h = reinterpret_cast<const __half*>(raw);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] = __half2float(h[k]);
-      }
-    } else {
-      for (int k = 0; k < 16; ++k) {
-        const uint32_t i = i0 + k;
-        float x = 0.f;
-        if (i < n) {
-          if (DT == DT_F32) x = reinterpret_cast<const float*>(in)[i];
-          else if (DT == DT_BF16) x = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(in)[i]);
-          else x = __half2float(reinterpret_cast<const __half*>(in)[i]);
-        }
-        v[k] = x;
-      }
-    }
-    float4* a4 = reinterpret_cast<float4*>(acc + i0);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float4 o = first ? make_float4(0.f, 0.f, 0.f, 0.f) : a4[q];
-      o.x = first ? v[4 * q] : o.x + v[4 * q];
-      o.y = first ? v[4 * q + 1] : o.y + v[4 * q + 1];
-      o.z = first ? v[4 * q + 2] : o.z + v[4 * q + 2];
-      o.w = first ? v[4 * q + 3] : o.w + v[4 * q + 3];
-      a4[q] = o;
-    }
-  }
-}
-
 // Copies `bytes` from src to dst (both 16-B aligned) with the whole CTA:
 // 16-byte vectors, then the last bytes one per thread (never reads past src).
 LZ_DEV void cta_copy_bytes(char* dst, const char* src, uint32_t bytes) {
@@ -126,13 +78,174 @@ LZ_DEV void cta_copy_bytes(char* dst, const char* src, uint32_t bytes) {
   if (threadIdx.x < bytes - v) dst[v + threadIdx.x] = src[v + threadIdx.x];
 }
 
+// Values of unit u (16 elements, guarded against n) of a reduction source:
+// the caller's plain input, or a decoded record (raw plane + symbols in sm).
 template <int DT>
-LZ_DEV void store_rounded(const float* __restrict__ acc, uint32_t n, char* __restrict__ out) {
-  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const float a = acc[i];
-    if (DT == DT_F32) reinterpret_cast<float*>(out)[i] = a;
-    else if (DT == DT_BF16) reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(a);
-    else reinterpret_cast<__half*>(out)[i] = __float2half_rn(a);
+LZ_DEV void unit_plain(const char* __restrict__ in, uint32_t u, uint32_t n, float (&v)[16]) {
+  constexpr int ES = DT == DT_F32 ? 4 : 2;
+  const uint32_t i0 = u * 16;
+  if (i0 + 16 <= n) {
+    uint4 raw[ES];
+#pragma unroll
+    for (int q = 0; q < ES; ++q) raw[q] = ld_cg_v4(in + (size_t)i0 * ES + 16 * q);
+    if (DT == DT_F32) {
+      const float* f = reinterpret_cast<const float*>(raw);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[k] = f[k];
+    } else if (DT == DT_BF16) {
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(raw);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[k] = __bfloat162float(h[k]);
+    } else {
+      const __half* h = reinterpret_cast<const __half*>(raw);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[k] = __half2float(h[k]);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint32_t i = i0 + k;
+      float x = 0.f;
+      if (i < n) {
+        if (DT == DT_F32) x = reinterpret_cast<const float*>(in)[i];
+        else if (DT == DT_BF16) x = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(in)[i]);
+        else x = __half2float(reinterpret_cast<const __half*>(in)[i]);
+      }
+      v[k] = x;
+    }
+  }
+}
+
+LZ_DEV uint32_t word_of(const uint4& v, int i) { return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w)); }
+
+template <int DT>
+LZ_DEV void unit_rec(const char* __restrict__ raw, const DecSmem& sm, uint32_t u, uint32_t n, float (&v)[16]) {
+  using S = Split16<DT>;
+  constexpr int RB = DT == DT_F32 ? 3 : 1;
+  const bool full = (u + 1) * 16 <= n;
+  if (DT != DT_F32) {
+    // 16 symbols and 16 raw bytes as four words each; element k is byte k % 4 of word k / 4
+    uint4 sv, rv;
+    if (full) {
+      rv = ld_cg_v4(raw + (size_t)u * 16);
+      sv = *reinterpret_cast<const uint4*>(&sm.syms[u * 16]);
+    } else {
+      uint32_t sw[4] = {0, 0, 0, 0}, rwd[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t i = u * 16 + k;
+        if (i < n) {
+          sw[k / 4] |= (uint32_t)sm.syms[i] << (8 * (k % 4));
+          rwd[k / 4] |= (uint32_t)ld_cg_u8(raw + i) << (8 * (k % 4));
+        }
+      }
+      sv = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+      rv = make_uint4(rwd[0], rwd[1], rwd[2], rwd[3]);
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint32_t sb = (word_of(sv, k / 4) >> (8 * (k % 4))) & 0xFFu;
+      const uint32_t rb = (word_of(rv, k / 4) >> (8 * (k % 4))) & 0xFFu;
+      if (DT == DT_BF16)
+        v[k] = __uint_as_float((((rb & 0x80u) << 8) | (sb << 7) | (rb & 0x7Fu)) << 16);
+      else
+        v[k] = __half2float(__ushort_as_half((unsigned short)((sb << 8) | rb)));
+    }
+    return;
+  }
+  alignas(16) uint8_t rw[S::RAW_BYTES];
+  uint8_t sy[16];
+  if (full) {
+#pragma unroll
+    for (int q = 0; q < S::RAW_BYTES / 16; ++q)
+      reinterpret_cast<uint4*>(rw)[q] = ld_cg_v4(raw + (size_t)u * S::RAW_BYTES + 16 * q);
+    *reinterpret_cast<uint4*>(sy) = *reinterpret_cast<const uint4*>(&sm.syms[u * 16]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint32_t i = u * 16 + k;
+      sy[k] = i < n ? sm.syms[i] : 0;
+#pragma unroll
+      for (int q = 0; q < RB; ++q) rw[k * RB + q] = i < n ? ld_cg_u8(raw + (size_t)i * RB + q) : 0;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = elem_to_f32<DT>(sy[k], rw + k * RB);
+}
+
+// One source of a TG reduction: plain input elements, or a record whose
+// symbols are decoded in sm (raw plane at `raw`).
+struct RedSrc {
+  const char* plain;
+  const char* raw;
+};
+
+// One pass of the rank-order fp32 reduction of a TG of n elements: v = value
+// of source a (+ value of source b, the next rank, when b is given); then
+// sum = v (first pass) or acc + v, in that order, so the result equals the
+// sequential fp32 sum. Intermediate passes keep the sum in `acc` (fp32
+// scratch); the last pass stores it rounded once to the element type at
+// `out` (no separate rounding pass).
+template <int DT>
+LZ_DEV void reduce_pass(RedSrc a, const RedSrc* b, const DecSmem& sm, uint32_t n, float* __restrict__ acc,
+                        bool first, char* __restrict__ out) {
+  constexpr int ES = DT == DT_F32 ? 4 : 2;
+  const uint32_t units = (n + 15) / 16;
+  for (uint32_t u = threadIdx.x; u < units; u += blockDim.x) {
+    float v[16];
+    if (a.plain) unit_plain<DT>(a.plain, u, n, v);
+    else unit_rec<DT>(a.raw, sm, u, n, v);
+    if (b) {
+      float w[16];
+      if (b->plain) unit_plain<DT>(b->plain, u, n, w);
+      else unit_rec<DT>(b->raw, sm, u, n, w);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[k] = v[k] + w[k];
+    }
+    float4* a4 = reinterpret_cast<float4*>(acc + (size_t)u * 16);
+    if (!first) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 o = a4[q];
+        v[4 * q] = o.x + v[4 * q];
+        v[4 * q + 1] = o.y + v[4 * q + 1];
+        v[4 * q + 2] = o.z + v[4 * q + 2];
+        v[4 * q + 3] = o.w + v[4 * q + 3];
+      }
+    }
+    if (!out) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) a4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      continue;
+    }
+    const uint32_t i0 = u * 16;
+    if (i0 + 16 <= n) {
+      uint4 o[ES];
+      if (DT == DT_F32) {
+        float* f = reinterpret_cast<float*>(o);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) f[k] = v[k];
+      } else if (DT == DT_BF16) {
+        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(o);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) h[k] = __float2bfloat16_rn(v[k]);
+      } else {
+        __half* h = reinterpret_cast<__half*>(o);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) h[k] = __float2half_rn(v[k]);
+      }
+#pragma unroll
+      for (int q = 0; q < ES; ++q) st_v4(out + (size_t)i0 * ES + 16 * q, o[q]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t i = i0 + k;
+        if (i >= n) break;
+        if (DT == DT_F32) reinterpret_cast<float*>(out)[i] = v[k];
+        else if (DT == DT_BF16) reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v[k]);
+        else reinterpret_cast<__half*>(out)[i] = __float2half_rn(v[k]);
+      }
+    }
   }
 }
 
@@ -187,25 +300,40 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
     for (uint32_t t = b; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
       const uint64_t e0 = s0 + (uint64_t)t * TG_ELEMS;
-      for (int s = 0; s < W; ++s) {
-        if (s == me) {
-          accumulate_plain<DT>(p.in + e0 * ES, tn, acc, s == 0);
-        } else if (!wait_slot(rs_slot(me, s, t), 2, s)) {
-          return;
-        } else if (p.hybrid) {
-          accumulate_plain<DT>(rs_slot(me, s, t), tn, acc, s == 0);
-        } else {
-          const char* rec = rs_slot(me, s, t);
-          if (!decode_tg_syms<DT>(rec, p.cap, tn, sm.dec)) {
-            if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 2, s);
-            return;
+      char* out_tg = p.out + e0 * ES;
+      // Sources in rank order. The first two go in one pass when one of them
+      // is this rank's own input (one decoded record at a time); the last
+      // pass rounds straight into the output.
+      int s = 0;
+      while (s < W) {
+        const bool pair = s == 0 && (me == 0 || me == 1);
+        const int last = pair ? 1 : s;
+        // source of rank r: own input, or its record (waited for, symbols decoded)
+        auto source = [&](int r, RedSrc& out_src) -> bool {
+          if (r == me) {
+            out_src = RedSrc{p.in + e0 * ES, nullptr};
+            return true;
           }
-          merge_accumulate<DT>(rec + sizeof(TgHeader), sm.dec, tn, acc, s == 0);
-        }
+          if (!wait_slot(rs_slot(me, r, t), 2, r)) return false;
+          const char* rec = rs_slot(me, r, t);
+          if (p.hybrid) {
+            out_src = RedSrc{rec, nullptr};
+            return true;
+          }
+          if (!decode_tg_syms<DT>(rec, p.cap, tn, sm.dec)) {
+            if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 2, r);
+            return false;
+          }
+          out_src = RedSrc{nullptr, rec + sizeof(TgHeader)};
+          return true;
+        };
+        RedSrc a, b2;
+        if (!source(s, a)) return;
+        if (pair && !source(1, b2)) return;
+        reduce_pass<DT>(a, pair ? &b2 : nullptr, sm.dec, tn, acc, s == 0, last == W - 1 ? out_tg : nullptr);
         __syncthreads();
+        s = last + 1;
       }
-      store_rounded<DT>(acc, tn, p.out + e0 * ES);
-      __syncthreads();
       char* mine = ag_slot(c.heap[me], me, t);
       const uint32_t bytes = encode_tg<DT>(p.out + e0 * ES, tn, mine, sm.enc, LV);
       const uint32_t padded = pad16(bytes);
