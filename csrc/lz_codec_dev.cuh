@@ -21,13 +21,14 @@ using namespace lzc;
 constexpr int LZC_THREADS = 256;  // one warp per sub-block
 constexpr int LZC_MIN_BLOCKS = 3;  // 3 CTAs (24 warps) per SM: caps registers at 85
 constexpr int HREP = 4;            // histogram replicas per warp (lane & 3)
+constexpr int HSTRIDE = 256 + 8;   // replica stride in words: bin s of replica r sits in bank (s + 8r) % 32
 static_assert(LZC_THREADS / 32 == NSUB, "one warp per sub-block");
 
 struct EncSmem {
   uint8_t syms[TG_ELEMS];  // symbol plane of the TG
   union {
     uint8_t streams[NSUB][SUB_ELEMS];     // per-warp rANS output (states + words)
-    uint32_t counts[NSUB][HREP][256];     // per-warp histograms, HREP replicas (before encoding)
+    uint32_t counts[NSUB][HREP][HSTRIDE];  // per-warp histograms, HREP replicas (before encoding)
   } u;
   uint32_t hist[256];                     // reduced histogram
   EncSym tab[256];
@@ -68,43 +69,71 @@ LZ_DEV uint32_t lanemask_lt() {
 }
 
 // ---------------------------------------------------------------------------
-// split of 16 elements (one "unit") starting at element index e
+// split of 16 elements (one "unit") into 16 symbol bytes and the raw plane,
+// as 32-bit words: symbol k is byte k % 4 of sw[k / 4]; the raw bytes of the
+// unit (RAW_BYTES of them, in element order) are rw[0 .. RAW_BYTES / 4).
+// Two 16-bit elements are processed per word operation (bf16, fp16).
 // ---------------------------------------------------------------------------
+// two 2-byte lanes (bytes 0 and 2 of a and b) -> one word of 4 bytes
+LZ_DEV uint32_t pick_even_bytes(uint32_t a, uint32_t b) { return __byte_perm(a, b, 0x6420); }
+// bytes 0, 1 (or 2, 3) of x -> bytes 0 and 2 of the result, zero elsewhere
+LZ_DEV uint32_t spread_lo(uint32_t x) { return __byte_perm(x, 0u, 0x4140); }
+LZ_DEV uint32_t spread_hi(uint32_t x) { return __byte_perm(x, 0u, 0x4342); }
+LZ_DEV uint32_t word_of(const uint4& v, int i) { return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w)); }
+
 template <int DT>
 struct Split16;
 
 template <>
 struct Split16<DT_BF16> {
-  static constexpr int IN_VECS = 2, RAW_BYTES = 16;
-  LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t* raw) {
-    const uint16_t* h = reinterpret_cast<const uint16_t*>(v);
+  static constexpr int IN_VECS = 2, RAW_BYTES = 16, RW = 4;
+  // symbol = bits 14..7; raw = sign (bit 15) << 7 | mantissa (bits 6..0), per 16-bit lane
+  LZ_DEV static void split(const uint4 (&v)[IN_VECS], uint32_t (&sw)[4], uint32_t (&rw)[RW]) {
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      sym[k] = sym_bf16(h[k]);
-      raw[k] = raw_bf16(h[k]);
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t a = word_of(v[j / 2], 2 * (j % 2)), b = word_of(v[j / 2], 2 * (j % 2) + 1);
+      const uint32_t sa = (a >> 7) & 0x00FF00FFu, sb = (b >> 7) & 0x00FF00FFu;
+      const uint32_t ra = ((a >> 8) & 0x00800080u) | (a & 0x007F007Fu);
+      const uint32_t rb = ((b >> 8) & 0x00800080u) | (b & 0x007F007Fu);
+      sw[j] = pick_even_bytes(sa, sb);
+      rw[j] = pick_even_bytes(ra, rb);
     }
   }
-  LZ_DEV static void merge(const uint8_t* sym, const uint8_t* raw, uint4* v) {
-    uint16_t* h = reinterpret_cast<uint16_t*>(v);
+  LZ_DEV static uint32_t merge2(uint32_t s2, uint32_t r2) {
+    return ((r2 & 0x00800080u) << 8) | (s2 << 7) | (r2 & 0x007F007Fu);
+  }
+  LZ_DEV static void merge(const uint32_t (&sw)[4], const uint32_t (&rw)[RW], uint4 (&v)[IN_VECS]) {
+    uint32_t o[8];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) h[k] = merge_bf16(sym[k], raw[k]);
+    for (int j = 0; j < 4; ++j) {
+      o[2 * j] = merge2(spread_lo(sw[j]), spread_lo(rw[j]));
+      o[2 * j + 1] = merge2(spread_hi(sw[j]), spread_hi(rw[j]));
+    }
+    v[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    v[1] = make_uint4(o[4], o[5], o[6], o[7]);
   }
 };
 template <>
 struct Split16<DT_F16> {
-  static constexpr int IN_VECS = 2, RAW_BYTES = 16;
-  LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t* raw) {
-    const uint16_t* h = reinterpret_cast<const uint16_t*>(v);
+  static constexpr int IN_VECS = 2, RAW_BYTES = 16, RW = 4;
+  // symbol = high byte (sign, exponent, 2 mantissa bits); raw = low byte
+  LZ_DEV static void split(const uint4 (&v)[IN_VECS], uint32_t (&sw)[4], uint32_t (&rw)[RW]) {
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      sym[k] = sym_f16(h[k]);
-      raw[k] = raw_f16(h[k]);
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t a = word_of(v[j / 2], 2 * (j % 2)), b = word_of(v[j / 2], 2 * (j % 2) + 1);
+      sw[j] = __byte_perm(a, b, 0x7531);
+      rw[j] = __byte_perm(a, b, 0x6420);
     }
   }
-  LZ_DEV static void merge(const uint8_t* sym, const uint8_t* raw, uint4* v) {
-    uint16_t* h = reinterpret_cast<uint16_t*>(v);
+  LZ_DEV static void merge(const uint32_t (&sw)[4], const uint32_t (&rw)[RW], uint4 (&v)[IN_VECS]) {
+    uint32_t o[8];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) h[k] = merge_f16(sym[k], raw[k]);
+    for (int j = 0; j < 4; ++j) {
+      o[2 * j] = __byte_perm(rw[j], sw[j], 0x5140);
+      o[2 * j + 1] = __byte_perm(rw[j], sw[j], 0x7362);
+    }
+    v[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    v[1] = make_uint4(o[4], o[5], o[6], o[7]);
   }
 };
 template <>
@@ -112,69 +141,70 @@ struct Split16<DT_F32> {
   // raw plane: 3 little-endian bytes per element; four elements' 24-bit raws
   // fill three 32-bit words exactly (r0 | r1 << 24, r1 >> 8 | r2 << 16,
   // r2 >> 16 | r3 << 8), so the packing is done with word shifts
-  static constexpr int IN_VECS = 4, RAW_BYTES = 48;
-  LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t* raw) {
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(v);
-    uint32_t* rw = reinterpret_cast<uint32_t*>(raw);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) sym[k] = sym_f32(w[k]);
+  static constexpr int IN_VECS = 4, RAW_BYTES = 48, RW = 12;
+  LZ_DEV static void split(const uint4 (&v)[IN_VECS], uint32_t (&sw)[4], uint32_t (&rw)[RW]) {
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const uint32_t r0 = raw_f32(w[4 * g]), r1 = raw_f32(w[4 * g + 1]);
-      const uint32_t r2 = raw_f32(w[4 * g + 2]), r3 = raw_f32(w[4 * g + 3]);
+      const uint32_t w0 = v[g].x, w1 = v[g].y, w2 = v[g].z, w3 = v[g].w;
+      sw[g] = (uint32_t)sym_f32(w0) | ((uint32_t)sym_f32(w1) << 8) | ((uint32_t)sym_f32(w2) << 16) |
+              ((uint32_t)sym_f32(w3) << 24);
+      const uint32_t r0 = raw_f32(w0), r1 = raw_f32(w1), r2 = raw_f32(w2), r3 = raw_f32(w3);
       rw[3 * g] = r0 | (r1 << 24);
       rw[3 * g + 1] = (r1 >> 8) | (r2 << 16);
       rw[3 * g + 2] = (r2 >> 16) | (r3 << 8);
     }
   }
-  LZ_DEV static void merge(const uint8_t* sym, const uint8_t* raw, uint4* v) {
-    uint32_t* w = reinterpret_cast<uint32_t*>(v);
-    const uint32_t* rw = reinterpret_cast<const uint32_t*>(raw);
+  LZ_DEV static void merge(const uint32_t (&sw)[4], const uint32_t (&rw)[RW], uint4 (&v)[IN_VECS]) {
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const uint32_t a = rw[3 * g], b = rw[3 * g + 1], c = rw[3 * g + 2];
-      w[4 * g] = merge_f32(sym[4 * g], a & 0xFFFFFFu);
-      w[4 * g + 1] = merge_f32(sym[4 * g + 1], (a >> 24) | ((b & 0xFFFFu) << 8));
-      w[4 * g + 2] = merge_f32(sym[4 * g + 2], (b >> 16) | ((c & 0xFFu) << 16));
-      w[4 * g + 3] = merge_f32(sym[4 * g + 3], c >> 8);
+      const uint32_t a = rw[3 * g], b = rw[3 * g + 1], c = rw[3 * g + 2], s = sw[g];
+      v[g].x = merge_f32((uint8_t)s, a & 0xFFFFFFu);
+      v[g].y = merge_f32((uint8_t)(s >> 8), (a >> 24) | ((b & 0xFFFFu) << 8));
+      v[g].z = merge_f32((uint8_t)(s >> 16), (b >> 16) | ((c & 0xFFu) << 16));
+      v[g].w = merge_f32((uint8_t)(s >> 24), c >> 8);
     }
   }
 };
 template <>
 struct Split16<DT_U8> {
-  static constexpr int IN_VECS = 1, RAW_BYTES = 0;
-  LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t*) {
-    const uint8_t* b = reinterpret_cast<const uint8_t*>(v);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) sym[k] = b[k];
+  static constexpr int IN_VECS = 1, RAW_BYTES = 0, RW = 1;
+  LZ_DEV static void split(const uint4 (&v)[IN_VECS], uint32_t (&sw)[4], uint32_t (&rw)[RW]) {
+    sw[0] = v[0].x, sw[1] = v[0].y, sw[2] = v[0].z, sw[3] = v[0].w;
+    rw[0] = 0;
   }
-  LZ_DEV static void merge(const uint8_t* sym, const uint8_t*, uint4* v) {
-    uint8_t* b = reinterpret_cast<uint8_t*>(v);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) b[k] = sym[k];
+  LZ_DEV static void merge(const uint32_t (&sw)[4], const uint32_t (&)[RW], uint4 (&v)[IN_VECS]) {
+    v[0] = make_uint4(sw[0], sw[1], sw[2], sw[3]);
   }
 };
 
 template <int DT>
 struct SplitPair16 {  // 16 fp8 pairs (32 bytes) <-> 16 container elements
-  static constexpr int IN_VECS = 2, RAW_BYTES = 16;
-  LZ_DEV static void split(const uint4* v, uint8_t* sym, uint8_t* raw) {
-    const uint8_t* b = reinterpret_cast<const uint8_t*>(v);
+  static constexpr int IN_VECS = 2, RAW_BYTES = 16, RW = 4;
+  LZ_DEV static void split(const uint4 (&v)[IN_VECS], uint32_t (&sw)[4], uint32_t (&rw)[RW]) {
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
-      const uint16_t u = DT == DT_E4M3P ? pack_e4m3(b[2 * k], b[2 * k + 1]) : pack_e5m2(b[2 * k], b[2 * k + 1]);
-      sym[k] = sym_bf16(u);
-      raw[k] = raw_bf16(u);
+      const uint32_t w = word_of(v[k / 8], (k % 8) / 2);
+      const uint8_t a = (uint8_t)(w >> (16 * (k % 2))), b = (uint8_t)(w >> (16 * (k % 2) + 8));
+      const uint16_t u = DT == DT_E4M3P ? pack_e4m3(a, b) : pack_e5m2(a, b);
+      if (k % 4 == 0) sw[k / 4] = 0, rw[k / 4] = 0;
+      sw[k / 4] |= (uint32_t)sym_bf16(u) << (8 * (k % 4));
+      rw[k / 4] |= (uint32_t)raw_bf16(u) << (8 * (k % 4));
     }
   }
-  LZ_DEV static void merge(const uint8_t* sym, const uint8_t* raw, uint4* v) {
-    uint8_t* b = reinterpret_cast<uint8_t*>(v);
+  LZ_DEV static void merge(const uint32_t (&sw)[4], const uint32_t (&rw)[RW], uint4 (&v)[IN_VECS]) {
+    uint32_t o[8];
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
-      const uint16_t u = merge_bf16(sym[k], raw[k]);
-      if (DT == DT_E4M3P) unpack_e4m3(u, &b[2 * k], &b[2 * k + 1]);
-      else unpack_e5m2(u, &b[2 * k], &b[2 * k + 1]);
+      const uint16_t u = merge_bf16((uint8_t)(sw[k / 4] >> (8 * (k % 4))), (uint8_t)(rw[k / 4] >> (8 * (k % 4))));
+      uint8_t a, b;
+      if (DT == DT_E4M3P) unpack_e4m3(u, &a, &b);
+      else unpack_e5m2(u, &a, &b);
+      const uint32_t pair = (uint32_t)a | ((uint32_t)b << 8);
+      if (k % 2 == 0) o[k / 2] = pair;
+      else o[k / 2] |= pair << 16;
     }
+    v[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    v[1] = make_uint4(o[4], o[5], o[6], o[7]);
   }
 };
 template <>
@@ -754,7 +784,7 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
   const uint32_t raw_bytes = pad16(n * RB);
   char* raw_dst = dst + sizeof(TgHeader);
 
-  for (uint32_t k = tid; k < NSUB * HREP * 256; k += blockDim.x) (&sm.u.counts[0][0][0])[k] = 0;
+  for (uint32_t k = tid; k < NSUB * HREP * HSTRIDE; k += blockDim.x) (&sm.u.counts[0][0][0])[k] = 0;
   __syncthreads();
   // 1. split + histogram (+ raw plane straight to the destination)
   const uint32_t units = n / 16;
@@ -768,7 +798,7 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
   for (uint32_t u0 = 0; u0 < units; u0 += blockDim.x) {  // block-uniform trip count
     const uint32_t u = u0 + tid;
     const bool act = u < units;
-    uint8_t sy[16];
+    uint32_t sw[4];
     if (act) {
       uint4 v[S::IN_VECS];
 #pragma unroll
@@ -778,21 +808,23 @@ LZ_DEV uint32_t encode_tg(const char* __restrict__ in, uint32_t n, char* __restr
 #pragma unroll
         for (int q = 0; q < S::IN_VECS; ++q) nxt[q] = ld_cg_v4(in + (size_t)un * 16 * ES + 16 * q);
       }
-      alignas(16) uint8_t rw[S::RAW_BYTES > 0 ? S::RAW_BYTES : 16];
-      S::split(v, sy, rw);
-      *reinterpret_cast<uint4*>(&sm.syms[u * 16]) = *reinterpret_cast<const uint4*>(sy);
+      uint32_t rw[S::RW];
+      S::split(v, sw, rw);
+      *reinterpret_cast<uint4*>(&sm.syms[u * 16]) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
       if (RB > 0) {
 #pragma unroll
         for (int q = 0; q < S::RAW_BYTES / 16; ++q)
-          st_v4(raw_dst + (size_t)u * S::RAW_BYTES + 16 * q, reinterpret_cast<const uint4*>(rw)[q]);
+          st_v4(raw_dst + (size_t)u * S::RAW_BYTES + 16 * q,
+                make_uint4(rw[4 * q], rw[4 * q + 1], rw[4 * q + 2], rw[4 * q + 3]));
       }
     }
     // replicated per-warp histograms: one shared atomic per symbol, lanes
-    // spread over HREP copies to cut same-address serialisation
+    // spread over HREP copies (padded apart by 8 banks) to cut same-address
+    // and same-bank serialisation
     if (act) {
       uint32_t* h = sm.u.counts[warp][lane & (HREP - 1)];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) atomicAdd(&h[sy[k]], 1u);
+      for (int k = 0; k < 16; ++k) atomicAdd(&h[(sw[k / 4] >> (8 * (k % 4))) & 0xFFu], 1u);
     }
   }
   // tail elements (n % 16) and the zero padding of the raw plane
@@ -1102,33 +1134,33 @@ LZ_DEV void merge_store(const char* __restrict__ raw, const DecSmem& sm, uint32_
   const uint32_t tid = threadIdx.x, bd = blockDim.x;
   const uint32_t units = n / 16;
   uint32_t u = tid;
-  for (; u + (NB - 1) * bd < units; u += NB * bd) {
-    alignas(16) uint8_t rw[NB][RV > 0 ? S::RAW_BYTES : 16];
+  auto merge_unit = [&](uint32_t uu, const uint32_t (&rw)[S::RW]) {
+    const uint4 sv = *reinterpret_cast<const uint4*>(&sm.syms[uu * 16]);
+    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+    uint4 v[S::IN_VECS];
+    S::merge(sw, rw, v);
 #pragma unroll
-    for (int b = 0; b < NB; ++b)
+    for (int q = 0; q < S::IN_VECS; ++q) st_v4(out + (size_t)uu * 16 * ES + 16 * q, v[q]);
+  };
+  auto load_raw = [&](uint32_t uu, uint32_t (&rw)[S::RW]) {
+    rw[0] = 0;
 #pragma unroll
-      for (int q = 0; q < RV; ++q)
-        reinterpret_cast<uint4*>(rw[b])[q] = ld_cg_v4(raw + (size_t)(u + b * bd) * S::RAW_BYTES + 16 * q);
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      const uint32_t ub = u + b * bd;
-      uint4 sv = *reinterpret_cast<const uint4*>(&sm.syms[ub * 16]);
-      uint4 v[S::IN_VECS];
-      S::merge(reinterpret_cast<const uint8_t*>(&sv), rw[b], v);
-#pragma unroll
-      for (int q = 0; q < S::IN_VECS; ++q) st_v4(out + (size_t)ub * 16 * ES + 16 * q, v[q]);
+    for (int q = 0; q < RV; ++q) {
+      const uint4 x = ld_cg_v4(raw + (size_t)uu * S::RAW_BYTES + 16 * q);
+      rw[4 * q] = x.x, rw[4 * q + 1] = x.y, rw[4 * q + 2] = x.z, rw[4 * q + 3] = x.w;
     }
+  };
+  for (; u + (NB - 1) * bd < units; u += NB * bd) {
+    uint32_t rw[NB][S::RW];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) load_raw(u + b * bd, rw[b]);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) merge_unit(u + b * bd, rw[b]);
   }
   for (; u < units; u += bd) {
-    alignas(16) uint8_t rw[RV > 0 ? S::RAW_BYTES : 16];
-#pragma unroll
-    for (int q = 0; q < RV; ++q)
-      reinterpret_cast<uint4*>(rw)[q] = ld_cg_v4(raw + (size_t)u * S::RAW_BYTES + 16 * q);
-    uint4 sv = *reinterpret_cast<const uint4*>(&sm.syms[u * 16]);
-    uint4 v[S::IN_VECS];
-    S::merge(reinterpret_cast<const uint8_t*>(&sv), rw, v);
-#pragma unroll
-    for (int q = 0; q < S::IN_VECS; ++q) st_v4(out + (size_t)u * 16 * ES + 16 * q, v[q]);
+    uint32_t rw[S::RW];
+    load_raw(u, rw);
+    merge_unit(u, rw);
   }
   if (tid < n - units * 16) {
     const uint32_t i = units * 16 + tid;

@@ -5,7 +5,7 @@
 // between phases, so a CTA decodes and reduces its table groups while other
 // CTAs are still encoding theirs; bounded waits):
 //   1. RS encode+push: every table group (TG) of every peer's slice is
-//      split + rANS-encoded by this GPU and the record is written straight
+//      split + encoded (rANS or PACK level) by this GPU and the record is written straight
 //      into the peer's receive slot (peer stores over NVLink): only the
 //      compressed bytes cross the link, no staging copy, no size exchange.
 //   2. decode+reduce: the owner decodes the W-1 incoming records of each of
@@ -18,20 +18,29 @@
 //      slices straight into its output.
 // Records are never truncated: a TG that does not compress is stored RAW.
 // Every slot is followed by a 16-byte footer whose first word is the slot's
-// ready flag: the call epoch mixed with a 64-bit constant, stored with release
+// ready flag: the call epoch and chunk index mixed with a 64-bit constant, stored with release
 // semantics after the CTA's record stores and matched exactly (the stage is
 // shared with other algorithms, so a footer may hold stale data of any
-// value; a small integer or all-zero word can never match). Table group t is always handled by CTA t mod G on every
-// rank, so the start barrier of CTA b (every rank's CTA b has finished the
-// previous call) is what keeps a new call from overwriting slots the
-// previous one still reads.
+// value; a small integer or all-zero word can never match).
+// Chunks: every slice is processed in chunks of C table groups (C = all of
+// them unless the caller asks for chunks); within chunk k, table group t is
+// handled by CTA (t - kC) mod G on every rank, and a chunked call keeps two
+// chunks' slots (a ring), so its stage is bounded by the chunk size. A CTA
+// starts chunk k + 2 only after every rank's same-index CTA has published
+// that it finished chunk k (a progress word per CTA and peer), which frees
+// the ring slots; chunks k and k + 1 are in flight together. The start
+// barrier of CTA b (every rank's CTA b has finished the previous call) keeps
+// a new call from overwriting slots the previous one still reads.
 //
 // Reference behaviour being re-designed: the compressed two-shot all-to-all
 // ("LZip two-shot", single_node_nccl_allreduce_benchmark/compressed_twoshot_allreduce.py:126-247),
 // which compresses with dietgpu, sends a fixed 0.65-ratio prefix with NCCL
 // (silently truncating streams that do not fit, :177-178) and decompresses in
-// separate launches; and the compressed P2P hybrid
-// (single_node_nccl_allreduce_benchmark/compressed_p2p_allreduce.py:54-188).
+// separate launches; the compressed P2P hybrid
+// (single_node_nccl_allreduce_benchmark/compressed_p2p_allreduce.py:54-188);
+// and the double-buffered chunk pipeline of the compressed send/recv
+// allreduce (single_node_nccl_allreduce_benchmark/compressed_sendrecv_allreduce.py:41-231),
+// here a ring of two chunks' slots inside one launch.
 #include "lz_codec_dev.cuh"
 #include "lz_internal.h"
 
@@ -53,6 +62,10 @@ struct CzParams {
   float* acc;          // local fp32 scratch, TG_ELEMS per CTA
   int use_mc;          // publish AG records with multimem.st
   int hybrid;          // reduce-scatter moves raw bytes; only the all-gather is compressed
+  uint32_t chunk_tgs;  // TGs per slice per chunk (C); every slice is processed in chunks of C TGs
+  uint32_t nchunks;    // ceil(ntg_max / C)
+  uint32_t nslots;     // slots per source: ntg_max (one chunk) or 2 C (a ring of two chunks)
+  size_t prog_off;     // heap offset: chunk progress flags [LZ_MAX_BLOCKS][LZ_MAX_RANKS]
 };
 
 union CzSmem {
@@ -115,8 +128,6 @@ LZ_DEV void unit_plain(const char* __restrict__ in, uint32_t u, uint32_t n, floa
     }
   }
 }
-
-LZ_DEV uint32_t word_of(const uint4& v, int i) { return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w)); }
 
 template <int DT>
 LZ_DEV void unit_rec(const char* __restrict__ raw, const DecSmem& sm, uint32_t u, uint32_t n, float (&v)[16]) {
@@ -256,34 +267,65 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
   constexpr int ES = DT == DT_F32 ? 4 : 2;
   const unsigned long long epoch = epoch_read(c);
   const int W = c.world, me = c.rank, G = gridDim.x, b = blockIdx.x;
-  auto rs_slot = [&](int rank_heap, int src, uint32_t t) {
-    return c.heap[rank_heap] + p.rs_off + ((size_t)src * p.ntg_max + t) * p.sstride;
+  // slot of slice-local TG t in chunk k: its own slot (one chunk) or ring
+  // position (k & 1) * C + (t - k * C) (two chunks in flight)
+  const uint32_t C = p.chunk_tgs;
+  auto ring = [&](uint32_t t, uint32_t k) { return p.nchunks > 1 ? (k & 1u) * C + (t - k * C) : t; };
+  auto rs_slot = [&](int rank_heap, int src, uint32_t t, uint32_t k) {
+    return c.heap[rank_heap] + p.rs_off + ((size_t)src * p.nslots + ring(t, k)) * p.sstride;
   };
-  auto ag_slot = [&](char* base, int owner, uint32_t t) {
-    return base + p.ag_off + ((size_t)owner * p.ntg_max + t) * p.sstride;
+  auto ag_slot = [&](char* base, int owner, uint32_t t, uint32_t k) {
+    return base + p.ag_off + ((size_t)owner * p.nslots + ring(t, k)) * p.sstride;
   };
   auto flag_of = [&](char* slot) { return reinterpret_cast<unsigned long long*>(slot + p.cap); };
-  const unsigned long long ready = (epoch + 1ull) ^ 0x9E3779B97F4A7C15ull;
+  // ready value of a slot: distinct for every (call, chunk), mixed with a
+  // constant so that stale data of other algorithms never matches
+  auto ready_of = [&](uint32_t k) {
+    return (((epoch + 1ull) << 24) + (unsigned long long)k) ^ 0x9E3779B97F4A7C15ull;
+  };
+  unsigned long long ready = ready_of(0);
   __shared__ int s_wfail;
+  // chunk progress: prog[b][src] on this rank = chunks CTA b of rank src finished
+  auto prog = [&](int rank_heap, int src) {
+    return reinterpret_cast<unsigned long long*>(c.heap[rank_heap] + p.prog_off) + (size_t)b * LZ_MAX_RANKS + src;
+  };
+  if (p.nchunks > 2 && threadIdx.x < (unsigned)W) *prog(me, threadIdx.x) = 0ull;
   // CTA-wide bounded wait for a slot flag (thread 0 polls)
   auto wait_slot = [&](char* slot, int phase, int peer) {
     if (threadIdx.x == 0) s_wfail = lz_wait_eq(c, flag_of(slot), ready, phase, peer) ? 0 : 1;
     __syncthreads();
     return s_wfail == 0;
   };
-  // every rank's CTA b has finished the previous call
+  // every rank's CTA b has finished the previous call (and has cleared its
+  // progress row: no progress flag of this call is written before this point)
   if (!block_barrier(c, epoch, 1)) return;
+
+  for (uint32_t ck = 0; ck < p.nchunks; ++ck) {
+  ready = ready_of(ck);
+  const uint32_t t0 = ck * C, t1 = t0 + C;  // slice-local TG range of the chunk
+  // ring slots of chunk ck were last used by chunk ck - 2: every rank's CTA b
+  // must have finished it (bounded wait, like a barrier)
+  if (ck >= 2) {
+    __shared__ int s_pfail;
+    if (threadIdx.x == 0) s_pfail = 0;
+    __syncthreads();
+    if (threadIdx.x < (unsigned)W && (int)threadIdx.x != me &&
+        !lz_wait_ge(c, prog(me, threadIdx.x), ck - 1, 4, threadIdx.x))
+      s_pfail = 1;
+    __syncthreads();
+    if (s_pfail) return;
+  }
 
   // 1. encode my input's TGs of every peer's slice into that peer's RS slots
   //    (hybrid: copy them raw; the reduce-scatter then pays no codec work)
   for (int k = 1; k < W; ++k) {
     const int dst = (me + k) % W;
     const uint64_t s0 = slice_begin(p, dst), sl = slice_len(p, dst);
-    const uint32_t nt = ntg_of(p, dst);
-    for (uint32_t t = b; t < nt; t += G) {
+    const uint32_t nt = min(ntg_of(p, dst), t1);
+    for (uint32_t t = t0 + b; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
       const char* src = p.in + (s0 + (uint64_t)t * TG_ELEMS) * ES;
-      char* slot = rs_slot(dst, me, t);
+      char* slot = rs_slot(dst, me, t, ck);
       if (p.hybrid) cta_copy_bytes(slot, src, tn * ES);
       else encode_tg<DT>(src, tn, slot, sm.enc, LV);
       publish_block_writes(c);
@@ -294,10 +336,9 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
   // 2. decode + reduce (rank order, fp32) + store + re-encode + publish
   {
     const uint64_t s0 = slice_begin(p, me), sl = slice_len(p, me);
-    const uint32_t nt = ntg_of(p, me);
+    const uint32_t nt = min(ntg_of(p, me), t1);
     float* acc = p.acc + (size_t)b * TG_ELEMS;
-    __shared__ int s_bad;
-    for (uint32_t t = b; t < nt; t += G) {
+    for (uint32_t t = t0 + b; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
       const uint64_t e0 = s0 + (uint64_t)t * TG_ELEMS;
       char* out_tg = p.out + e0 * ES;
@@ -314,8 +355,8 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
             out_src = RedSrc{p.in + e0 * ES, nullptr};
             return true;
           }
-          if (!wait_slot(rs_slot(me, r, t), 2, r)) return false;
-          const char* rec = rs_slot(me, r, t);
+          if (!wait_slot(rs_slot(me, r, t, ck), 2, r)) return false;
+          const char* rec = rs_slot(me, r, t, ck);
           if (p.hybrid) {
             out_src = RedSrc{rec, nullptr};
             return true;
@@ -334,11 +375,11 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
         __syncthreads();
         s = last + 1;
       }
-      char* mine = ag_slot(c.heap[me], me, t);
+      char* mine = ag_slot(c.heap[me], me, t, ck);
       const uint32_t bytes = encode_tg<DT>(p.out + e0 * ES, tn, mine, sm.enc, LV);
       const uint32_t padded = pad16(bytes);
       if (p.use_mc) {
-        char* mc = ag_slot(c.heap_mc, me, t);
+        char* mc = ag_slot(c.heap_mc, me, t, ck);
         for (uint32_t o = threadIdx.x * 16; o < padded; o += blockDim.x * 16)
           multimem_st_v4(mc + o, ld_cg_v4(mine + o));
         publish_block_writes(c);
@@ -348,35 +389,42 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
         }
       } else {
         for (int k = 1; k < W; ++k) {
-          char* dstp = ag_slot(c.heap[(me + k) % W], me, t);
+          char* dstp = ag_slot(c.heap[(me + k) % W], me, t, ck);
           for (uint32_t o = threadIdx.x * 16; o < padded; o += blockDim.x * 16)
             st_v4(dstp + o, ld_cg_v4(mine + o));
         }
         publish_block_writes(c);
         if (threadIdx.x == 0)
-          for (int k = 1; k < W; ++k) st_release_sys(flag_of(ag_slot(c.heap[(me + k) % W], me, t)), ready);
+          for (int k = 1; k < W; ++k) st_release_sys(flag_of(ag_slot(c.heap[(me + k) % W], me, t, ck)), ready);
       }
       __syncthreads();
     }
-    (void)s_bad;
   }
 
   // 3. decode the other owners' reduced TGs into my output
   for (int k = 1; k < W; ++k) {
     const int own = (me + W - k) % W;
     const uint64_t s0 = slice_begin(p, own), sl = slice_len(p, own);
-    const uint32_t nt = ntg_of(p, own);
-    for (uint32_t t = b; t < nt; t += G) {
+    const uint32_t nt = min(ntg_of(p, own), t1);
+    for (uint32_t t = t0 + b; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
-      if (!wait_slot(ag_slot(c.heap[me], own, t), 3, own)) return;
+      if (!wait_slot(ag_slot(c.heap[me], own, t, ck), 3, own)) return;
       if (p.use_mc) fence_proxy_alias();  // the record arrived through the multicast mapping
-      if (!decode_tg<DT>(ag_slot(c.heap[me], own, t), p.cap, tn, p.out + (s0 + (uint64_t)t * TG_ELEMS) * ES,
+      if (!decode_tg<DT>(ag_slot(c.heap[me], own, t, ck), p.cap, tn, p.out + (s0 + (uint64_t)t * TG_ELEMS) * ES,
                          sm.dec)) {
         if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 3, own);
         return;
       }
     }
   }
+  // chunk ck done on this CTA: peers may refill its ring slots with chunk
+  // ck + 2 (only progress that some peer waits for is published, so no write
+  // of this call is still in flight when the next call clears the row)
+  if (ck + 2 < p.nchunks) {
+    publish_block_writes(c);
+    if (threadIdx.x < (unsigned)W && (int)threadIdx.x != me) st_release_sys(prog(threadIdx.x, me), ck + 1);
+  }
+  }  // chunks
   epoch_advance(c);
 }
 
@@ -416,12 +464,43 @@ void* cz_kernel_for(int dtype, bool emu, int flags) {
 
 }  // namespace
 
-// Bytes of the compressed-allreduce staging region for n elements.
-extern "C" size_t lz_cz_stage_bytes(size_t n, int dtype, int world, int nblocks) {
-  const uint64_t slice = ((n + world - 1) / world + 15) / 16 * 16;
-  const uint64_t ntg = num_tgs(slice);
+// Geometry of a call: TGs per slice, TGs per slice per chunk, chunks, slots
+// per source. chunk_elems = elements of the whole vector per chunk (0 or
+// >= n: one chunk, every TG its own slot); a chunked call keeps two chunks'
+// slots in flight (ring), so its stage is bounded by the chunk, not by n.
+struct CzGeom {
+  uint64_t slice;
+  uint32_t ntg, chunk_tgs, nchunks, nslots;
+};
+static CzGeom cz_geom(size_t n, int world, size_t chunk_elems) {
+  CzGeom g;
+  g.slice = ((n + world - 1) / world + 15) / 16 * 16;
+  g.ntg = (uint32_t)num_tgs(g.slice);
+  uint64_t per_slice = chunk_elems ? (chunk_elems + world - 1) / world : 0;
+  uint32_t c = per_slice ? (uint32_t)num_tgs(per_slice) : g.ntg;
+  if (c < 1) c = 1;
+  if (c >= g.ntg) c = g.ntg;
+  g.chunk_tgs = c;
+  g.nchunks = g.ntg ? (g.ntg + c - 1) / c : 1;
+  if (g.nchunks < 1) g.nchunks = 1;
+  g.nslots = g.nchunks > 1 ? 2 * c : g.ntg;
+  return g;
+}
+
+static size_t cz_stage_bytes(size_t n, int dtype, int world, int nblocks, size_t chunk_elems) {
+  const CzGeom g = cz_geom(n, world, chunk_elems);
   const uint64_t sstride = tg_capacity(dtype) + 16;  // record capacity + flag footer
-  return 2 * (size_t)world * ntg * sstride + (size_t)nblocks * TG_ELEMS * 4 + 256;
+  const size_t prog = (size_t)LZ_MAX_BLOCKS * LZ_MAX_RANKS * 8;
+  return 2 * (size_t)world * g.nslots * sstride + (size_t)nblocks * TG_ELEMS * 4 + prog + 256;
+}
+
+// Bytes of the compressed-allreduce staging region for n elements (one chunk).
+extern "C" size_t lz_cz_stage_bytes(size_t n, int dtype, int world, int nblocks) {
+  return cz_stage_bytes(n, dtype, world, nblocks, 0);
+}
+// The same for calls processed in chunks of chunk_elems elements.
+extern "C" size_t lz_cz_stage_bytes_chunked(size_t n, int dtype, int world, int nblocks, size_t chunk_elems) {
+  return cz_stage_bytes(n, dtype, world, nblocks, chunk_elems);
 }
 
 extern "C" int lz_cz_default_blocks(LzComm* c) { return c->sm_count * 3; }
@@ -430,7 +509,7 @@ extern "C" int lz_cz_default_blocks(LzComm* c) { return c->sm_count * 3; }
 // multicast object exists), bit 1 hybrid (raw reduce-scatter), bit 2 PACK
 // codec level (table codes; faster than rANS, lower ratio).
 static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dtype, int G,
-                   int flags, CzParams* out_p) {
+                   int flags, size_t chunk_elems, CzParams* out_p) {
   const int W = c->dev.world;
   if (dtype != LZ_F32 && dtype != LZ_F16 && dtype != LZ_BF16) {
     lz_set_error("compressed allreduce: dtype %d not supported (float types only)", dtype);
@@ -440,24 +519,32 @@ static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dty
     lz_set_error("compressed allreduce needs 16-byte aligned buffers");
     return LZE_ARG;
   }
+  const CzGeom g = cz_geom(n, W, chunk_elems);
   CzParams p;
   memset(&p, 0, sizeof(p));
   p.in = static_cast<const char*>(in);
   p.out = static_cast<char*>(out);
   p.n = n;
-  p.slice = ((n + W - 1) / W + 15) / 16 * 16;
-  p.ntg_max = (uint32_t)num_tgs(p.slice);
+  p.slice = g.slice;
+  p.ntg_max = g.ntg;
+  p.chunk_tgs = g.chunk_tgs;
+  p.nchunks = g.nchunks;
+  p.nslots = g.nslots;
   p.cap = tg_capacity(dtype);
   p.sstride = p.cap + 16;
-  const size_t need = lz_cz_stage_bytes(n, dtype, W, G);
+  const size_t need = cz_stage_bytes(n, dtype, W, G, chunk_elems);
   if (need > c->stage_bytes) {
-    lz_set_error("compressed allreduce: stage needs %zu bytes, communicator has %zu (raise stage_bytes)",
+    lz_set_error("compressed allreduce: stage needs %zu bytes, communicator has %zu (raise stage_bytes "
+                 "or process the call in chunks)",
                  need, c->stage_bytes);
     return LZE_ARG;
   }
+  const size_t slots = (size_t)W * p.nslots * p.sstride;
   p.rs_off = c->stage_off;
-  p.ag_off = c->stage_off + (size_t)W * p.ntg_max * p.sstride;
-  p.acc = reinterpret_cast<float*>(c->dev.heap[c->dev.rank] + p.ag_off + (size_t)W * p.ntg_max * p.sstride);
+  p.ag_off = c->stage_off + slots;
+  const size_t acc_off = p.ag_off + slots;
+  p.acc = reinterpret_cast<float*>(c->dev.heap[c->dev.rank] + acc_off);
+  p.prog_off = (acc_off + (size_t)G * TG_ELEMS * 4 + 15) / 16 * 16;
   p.use_mc = ((flags & 1) && c->dev.heap_mc) ? 1 : 0;
   p.hybrid = (flags & 2) ? 1 : 0;
   *out_p = p;
@@ -466,9 +553,9 @@ static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dty
 
 // flags: bit 0 multicast all-gather, bit 1 hybrid (raw reduce-scatter, the
 // compressed P2P hybrid of the reference's compressed_p2p_allreduce.py:54-188),
-// bit 2 PACK codec level.
-extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, size_t n, int dtype,
-                                       int nblocks, int flags, cudaStream_t s) {
+// bit 2 PACK codec level. chunk_elems: see cz_geom (0: one chunk).
+extern "C" int lz_compressed_allreduce_chunked(LzComm* c, const void* in, void* out, size_t n, int dtype,
+                                               int nblocks, int flags, size_t chunk_elems, cudaStream_t s) {
   const int W = c->dev.world;
   const size_t es = dtype == LZ_F32 ? 4 : 2;
   if (W == 1) {
@@ -478,7 +565,7 @@ extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, siz
   int G = nblocks > 0 ? nblocks : lz_cz_default_blocks(c);
   if (G > LZ_MAX_BLOCKS) G = LZ_MAX_BLOCKS;
   CzParams p;
-  int rc = cz_plan(c, in, out, n, dtype, G, flags, &p);
+  int rc = cz_plan(c, in, out, n, dtype, G, flags, chunk_elems, &p);
   if (rc) return rc;
   void* fn = cz_kernel_for(dtype, false, flags);
   const size_t smem = sizeof(CzSmem);
@@ -488,9 +575,15 @@ extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, siz
   return LZE_OK;
 }
 
+extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, size_t n, int dtype,
+                                       int nblocks, int flags, cudaStream_t s) {
+  return lz_compressed_allreduce_chunked(c, in, out, n, dtype, nblocks, flags, 0, s);
+}
+
 // Single-GPU emulation of the compressed allreduce over the R emulated ranks.
-extern "C" int lz_emu_compressed_allreduce(LzEmu* e, const void* const* ins, void* const* outs,
-                                           size_t n, int dtype, int nblocks, int flags, cudaStream_t s) {
+extern "C" int lz_emu_compressed_allreduce_chunked(LzEmu* e, const void* const* ins, void* const* outs,
+                                                   size_t n, int dtype, int nblocks, int flags,
+                                                   size_t chunk_elems, cudaStream_t s) {
   const int R = lz_emu_world(e);
   void* fn = cz_kernel_for(dtype, true, flags);
   const size_t smem = sizeof(CzSmem);
@@ -505,7 +598,7 @@ extern "C" int lz_emu_compressed_allreduce(LzEmu* e, const void* const* ins, voi
   }
   CzParams hp[LZ_MAX_RANKS];
   for (int r = 0; r < R; ++r) {
-    int rc = cz_plan(lz_emu_comm(e, r), ins[r], outs[r], n, dtype, G, flags & 2, &hp[r]);
+    int rc = cz_plan(lz_emu_comm(e, r), ins[r], outs[r], n, dtype, G, flags & 2, chunk_elems, &hp[r]);
     if (rc) return rc;
   }
   static_assert(sizeof(CzParams) * LZ_MAX_RANKS <= 4096, "param buffer");
@@ -516,4 +609,9 @@ extern "C" int lz_emu_compressed_allreduce(LzEmu* e, const void* const* ins, voi
   LZ_CUDA_TRY(cudaLaunchCooperativeKernel(fn, dim3(G, R), dim3(LZC_THREADS), args, smem, s));
   LZ_CUDA_TRY(cudaStreamSynchronize(s));
   return LZE_OK;
+}
+
+extern "C" int lz_emu_compressed_allreduce(LzEmu* e, const void* const* ins, void* const* outs,
+                                           size_t n, int dtype, int nblocks, int flags, cudaStream_t s) {
+  return lz_emu_compressed_allreduce_chunked(e, ins, outs, n, dtype, nblocks, flags, 0, s);
 }

@@ -11,9 +11,10 @@ Distributions: ``grad`` = N(0, 1e-3) (gradient-like); ``act`` = N(0, 1) with 1 %
 of the elements multiplied by 50 (activation-like with outliers); per rank
 from a fixed seed. SM budgets use CUDA green contexts (0 = whole GPU); the
 kernel grid is sized to what the budget keeps resident. ``--chunks-mb``
-processes the tensor as back-to-back calls on chunks of that size (0 = one
-call). ``extra_mem_bytes`` is the stage the native kernel needs for the
-largest call plus any torch allocations made by the call (NCCL: 0).
+processes the tensor in chunks of that size inside the one launch (a ring of
+two chunks' slots bounds the stage memory; 0 = one chunk). ``extra_mem_bytes``
+is the stage the native kernel needs for the call plus any torch allocations
+made by the call (NCCL: 0).
 The fp8 rows cast the tensor to e4m3fn / e5m2, and rank 0 sends it through the
 split+rANS transfer kernel (pair containers) to rank 1.
 
@@ -133,23 +134,19 @@ def main(argv=None):
                 st = streams[b]
                 nb = 3 * (st.sm_count if st is not None else sms)
                 for cmb, var in [(cm, vv) for cm in chunks for vv in a.variants.split(",")]:
-                    step = (cmb * MiB // 2) if cmb else n
                     if cmb and cmb * MiB >= nbytes:
                         continue
-                    parts = [(i, min(step, n - i)) for i in range(0, n, step)]
-
                     level = "pack" if var.endswith("_pack") else "ans"
                     ratio = ratios[level]
 
-                    def run(hybrid=var.startswith("hybrid"), level=level):
-                        for i, ln in parts:
-                            cz.compressed_allreduce(x[i:i + ln], y[i:i + ln], comm=comm, nblocks=nb, hybrid=hybrid,
-                                                    level=level)
+                    def run(hybrid=var.startswith("hybrid"), level=level, cb=cmb * MiB):
+                        cz.compressed_allreduce(x, y, comm=comm, nblocks=nb, hybrid=hybrid, level=level,
+                                                chunk_bytes=cb)
 
                     torch.cuda.reset_peak_memory_stats()
                     m0 = torch.cuda.memory_allocated()
                     ms = timed(run, st)
-                    extra = cz.stage_bytes_needed(step, torch.bfloat16, world, nb) + \
+                    extra = cz.stage_bytes_needed(n, torch.bfloat16, world, nb, chunk_elems=cmb * MiB // 2) + \
                         (torch.cuda.max_memory_allocated() - m0)
                     exact = bool(torch.equal(y, ref))
                     rows.append({**base, "sm_budget": b or sms, "chunk_mb": cmb, "variant": var,

@@ -45,25 +45,39 @@ _native_sigs.add_cuda({
                                 C.c_int, C.c_void_p),
     "lz_emu_compressed_allreduce": (C.c_int, C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                     C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_void_p),
+    "lz_cz_stage_bytes_chunked": (C.c_size_t, C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_size_t),
+    "lz_compressed_allreduce_chunked": (C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
+                                        C.c_int, C.c_int, C.c_size_t, C.c_void_p),
+    "lz_emu_compressed_allreduce_chunked": (C.c_int, C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                            C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p),
 })
 
 HDR = 16  # u64 stream size + u64 overflow flag
 
 
 # ----------------------------------------------------------------------------- native
-def stage_bytes_needed(n: int, dtype: torch.dtype, world: int, nblocks: int = 444) -> int:
-    return int(_native.cuda().lz_cz_stage_bytes(n, lz_dtype(dtype), world, nblocks))
+def stage_bytes_needed(n: int, dtype: torch.dtype, world: int, nblocks: int = 444, chunk_elems: int = 0) -> int:
+    """Stage bytes of a native compressed allreduce of n elements; with
+    ``chunk_elems`` > 0 the call runs in chunks of that many elements and
+    needs slots for two chunks only."""
+    return int(_native.cuda().lz_cz_stage_bytes_chunked(n, lz_dtype(dtype), world, nblocks, chunk_elems))
 
 
 @traced("compressed_allreduce")
 def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=None,
                          nblocks: int = 0, multicast: bool = True, stream=None,
-                         hybrid: bool = False, level="ans") -> torch.Tensor:
+                         hybrid: bool = False, level="ans", chunk_bytes: int = 0) -> torch.Tensor:
     """Sum-allreduce with lossless compression on the wire (native fused kernel).
 
     ``level``: codec level of the records, "ans" (rANS, best ratio) or "pack"
     (table codes: a few integer operations per element, ratio ~0.70 for bf16
     instead of ~0.67).
+
+    ``chunk_bytes`` > 0 processes the vector in chunks of that many bytes
+    inside the one launch: every slice moves chunk by chunk through a ring of
+    two chunks' slots, so the stage memory is bounded by the chunk size while
+    encoding, transfer and decoding of neighbouring chunks overlap (a CTA
+    starts chunk k + 2 as soon as every rank's same CTA has finished chunk k).
 
     ``hybrid=True`` is the compressed P2P hybrid: the reduce-scatter moves raw
     bytes and only the all-gather of the reduced slices is compressed, so each
@@ -79,10 +93,12 @@ def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=
         out = t
     s = stream or torch.cuda.current_stream(comm.device)
     nb = nblocks or comm.config.sm_budget
-    rc = comm._lib.lz_compressed_allreduce(comm.handle, t.data_ptr(), out.data_ptr(), t.numel(),
-                                           lz_dtype(t.dtype), nb,
-                                           int(multicast) | (2 if hybrid else 0) | (4 * codec.level_code(level)),
-                                           s.cuda_stream)
+    chunk_elems = chunk_bytes // t.element_size() if chunk_bytes else 0
+    rc = comm._lib.lz_compressed_allreduce_chunked(comm.handle, t.data_ptr(), out.data_ptr(), t.numel(),
+                                                   lz_dtype(t.dtype), nb,
+                                                   int(multicast) | (2 if hybrid else 0) |
+                                                   (4 * codec.level_code(level)),
+                                                   chunk_elems, s.cuda_stream)
     _native.check(rc, "compressed_allreduce")
     return out
 

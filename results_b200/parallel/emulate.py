@@ -62,16 +62,17 @@ class EmulatedWorld:
                                         s.cuda_stream)
         _native.check(rc, f"emulated allreduce[{algo}]")
 
-    def compressed_allreduce(self, ins, outs, nblocks: int = 0, hybrid: bool = False, level="ans"):
+    def compressed_allreduce(self, ins, outs, nblocks: int = 0, hybrid: bool = False, level="ans",
+                             chunk_elems: int = 0):
         from . import compressed  # noqa: F401  (declares the native signature)
         from ..ops import codec
 
         R = self.world
         arr_in = (C.c_void_p * R)(*[t.data_ptr() for t in ins])
         arr_out = (C.c_void_p * R)(*[t.data_ptr() for t in outs])
-        rc = self._lib.lz_emu_compressed_allreduce(self._emu, arr_in, arr_out, ins[0].numel(),
+        rc = self._lib.lz_emu_compressed_allreduce_chunked(self._emu, arr_in, arr_out, ins[0].numel(),
                                                    lz_dtype(ins[0].dtype), nblocks,
-                                                   (2 if hybrid else 0) | 4 * codec.level_code(level),
+                                                   (2 if hybrid else 0) | 4 * codec.level_code(level), chunk_elems,
                                                    torch.cuda.current_stream().cuda_stream)
         _native.check(rc, "emulated compressed allreduce")
 

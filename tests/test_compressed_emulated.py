@@ -69,3 +69,38 @@ def test_compressed_inplace_activation_like(worlds, level):
         acc += x.float()
     for r in range(R):
         assert torch.equal(bufs[r], acc.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("level", ["ans", "pack"])
+@pytest.mark.parametrize("hybrid", [False, True])
+@pytest.mark.parametrize("R", [2, 4])
+@pytest.mark.parametrize("chunk_tgs,nblocks", [(1, 3), (2, 8), (3, 2)])
+def test_compressed_allreduce_chunked_ring(worlds, R, hybrid, level, chunk_tgs, nblocks):
+    """In-launch chunks through a ring of two chunks' slots: slices of 6+ table
+    groups in chunks of 1-3 TGs, CTAs fewer or more than a chunk's TGs, three
+    calls in a row (progress flags are cleared per call), bit-exact."""
+    w = worlds[R]
+    n = 32768 * R * 6 + 48 * R + 16
+    outs = None
+    for it in range(3):
+        xs = _inputs(R, n, torch.bfloat16, seed=1000 * it + 10 * R + chunk_tgs)
+        outs = [torch.empty_like(x) for x in xs]
+        w.compressed_allreduce(xs, outs, nblocks=nblocks, hybrid=hybrid, level=level,
+                               chunk_elems=32768 * R * chunk_tgs)
+        torch.cuda.synchronize()
+        acc = xs[0].float().clone()
+        for x in xs[1:]:
+            acc += x.float()
+        ref = acc.to(torch.bfloat16)
+        for r in range(R):
+            assert w.status(r) == 0
+            assert torch.equal(outs[r].view(torch.uint8), ref.view(torch.uint8)), (it, r)
+
+
+def test_chunked_stage_is_bounded():
+    from results_b200.parallel import compressed as cz
+
+    n = 256 << 20  # 512 MiB of bf16
+    whole = cz.stage_bytes_needed(n, torch.bfloat16, 8, 444)
+    chunked = cz.stage_bytes_needed(n, torch.bfloat16, 8, 444, chunk_elems=(64 << 20) // 2)
+    assert chunked < whole / 3
