@@ -23,12 +23,13 @@
 // shared with other algorithms, so a footer may hold stale data of any
 // value; a small integer or all-zero word can never match).
 // Chunks: every slice is processed in chunks of C table groups (C = all of
-// them unless the caller asks for chunks); within chunk k, table group t is
-// handled by CTA (t - kC) mod G on every rank, and a chunked call keeps two
-// chunks' slots (a ring), so its stage is bounded by the chunk size. A CTA
-// starts chunk k + 2 only after every rank's same-index CTA has published
-// that it finished chunk k (a progress word per CTA and peer), which frees
-// the ring slots; chunks k and k + 1 are in flight together. The start
+// them unless the caller asks for chunks); table group t (slice-local index)
+// is handled by CTA t mod G on every rank in every chunk, so consecutive
+// chunks smaller than the grid still spread over all CTAs; a chunked call keeps
+// two chunks' slots (a ring), so its stage is bounded by the chunk size. A
+// CTA starts chunk k + 2 only after the CTA that used its ring slots in chunk
+// k has finished that chunk on every rank (progress words in the flag area),
+// so chunks k and k + 1 are in flight together. The start
 // barrier of CTA b (every rank's CTA b has finished the previous call) keeps
 // a new call from overwriting slots the previous one still reads.
 //
@@ -62,11 +63,17 @@ struct CzParams {
   float* acc;          // local fp32 scratch, TG_ELEMS per CTA
   int use_mc;          // publish AG records with multimem.st
   int hybrid;          // reduce-scatter moves raw bytes; only the all-gather is compressed
+  int stage_local;     // RS records are encoded into local memory, then pushed as 16-byte vectors
   uint32_t chunk_tgs;  // TGs per slice per chunk (C); every slice is processed in chunks of C TGs
   uint32_t nchunks;    // ceil(ntg_max / C)
   uint32_t nslots;     // slots per source: ntg_max (one chunk) or 2 C (a ring of two chunks)
-  size_t prog_off;     // heap offset: chunk progress flags [LZ_MAX_BLOCKS][LZ_MAX_RANKS]
 };
+
+// Chunk progress words [LZ_MAX_BLOCKS][LZ_MAX_RANKS] in the flag area (a
+// region of its own, written with monotonic values only).
+constexpr size_t kCzProgOff = 576u << 10;
+static_assert(kCzProgOff + (size_t)LZ_MAX_BLOCKS * LZ_MAX_RANKS * 8 <= kLzFlagsBytes,
+              "compressed-allreduce progress words exceed the flag area");
 
 union CzSmem {
   EncSmem enc;
@@ -82,6 +89,22 @@ LZ_DEV uint64_t slice_len(const CzParams& p, int s) {
   return e - b;
 }
 LZ_DEV uint32_t ntg_of(const CzParams& p, int s) { return (uint32_t)num_tgs(slice_len(p, s)); }
+
+// Copies `padded` bytes (multiple of 16, both 16-B aligned) with the whole CTA,
+// eight 16-byte loads in flight per thread (peer destinations).
+LZ_DEV void cta_push16(char* dst, const char* src, uint32_t padded) {
+  constexpr int U = 8;
+  const uint32_t step = blockDim.x * 16;
+  uint32_t o = threadIdx.x * 16;
+  for (; o + (U - 1) * step < padded; o += U * step) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) v[u] = ld_cg_v4(src + o + u * step);
+#pragma unroll
+    for (int u = 0; u < U; ++u) st_v4(dst + o + u * step, v[u]);
+  }
+  for (; o < padded; o += step) st_v4(dst + o, ld_cg_v4(src + o));
+}
 
 // Copies `bytes` from src to dst (both 16-B aligned) with the whole CTA:
 // 16-byte vectors, then the last bytes one per thread (never reads past src).
@@ -285,32 +308,36 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
   };
   unsigned long long ready = ready_of(0);
   __shared__ int s_wfail;
-  // chunk progress: prog[b][src] on this rank = chunks CTA b of rank src finished
-  auto prog = [&](int rank_heap, int src) {
-    return reinterpret_cast<unsigned long long*>(c.heap[rank_heap] + p.prog_off) + (size_t)b * LZ_MAX_RANKS + src;
+  // chunk progress: prog(r, blk, src) on rank r's heap = last chunk CTA blk of
+  // rank src finished, as ((epoch + 1) << 24) + chunk + 1 (monotonic across
+  // calls, so nothing is ever reset)
+  auto prog = [&](int rank_heap, uint32_t blk, int src) {
+    return reinterpret_cast<unsigned long long*>(c.heap[rank_heap] + kCzProgOff) + (size_t)blk * LZ_MAX_RANKS + src;
   };
-  if (p.nchunks > 2 && threadIdx.x < (unsigned)W) *prog(me, threadIdx.x) = 0ull;
+  auto done_value = [&](uint32_t k) { return ((epoch + 1ull) << 24) + (unsigned long long)k + 1ull; };
   // CTA-wide bounded wait for a slot flag (thread 0 polls)
   auto wait_slot = [&](char* slot, int phase, int peer) {
     if (threadIdx.x == 0) s_wfail = lz_wait_eq(c, flag_of(slot), ready, phase, peer) ? 0 : 1;
     __syncthreads();
     return s_wfail == 0;
   };
-  // every rank's CTA b has finished the previous call (and has cleared its
-  // progress row: no progress flag of this call is written before this point)
+  // every rank's CTA b has finished the previous call
   if (!block_barrier(c, epoch, 1)) return;
 
   for (uint32_t ck = 0; ck < p.nchunks; ++ck) {
   ready = ready_of(ck);
   const uint32_t t0 = ck * C, t1 = t0 + C;  // slice-local TG range of the chunk
-  // ring slots of chunk ck were last used by chunk ck - 2: every rank's CTA b
-  // must have finished it (bounded wait, like a barrier)
+  // TG t is handled by CTA t mod G: this CTA's first TG of the chunk
+  const uint32_t first = (uint32_t)((b + G - (int)(((uint64_t)ck * C) % G)) % G);
+  // The ring slots of this CTA's TGs were last used in chunk ck - 2 by CTA
+  // (b - 2C) mod G of every rank (consumer of the records, and this rank's own
+  // staging): wait until each of them has finished that chunk (bounded).
   if (ck >= 2) {
     __shared__ int s_pfail;
     if (threadIdx.x == 0) s_pfail = 0;
     __syncthreads();
-    if (threadIdx.x < (unsigned)W && (int)threadIdx.x != me &&
-        !lz_wait_ge(c, prog(me, threadIdx.x), ck - 1, 4, threadIdx.x))
+    const uint32_t prev = (uint32_t)((b + G - (int)((2ull * C) % G)) % G);
+    if (threadIdx.x < (unsigned)W && !lz_wait_ge(c, prog(me, prev, threadIdx.x), done_value(ck - 2), 4, threadIdx.x))
       s_pfail = 1;
     __syncthreads();
     if (s_pfail) return;
@@ -322,12 +349,21 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
     const int dst = (me + k) % W;
     const uint64_t s0 = slice_begin(p, dst), sl = slice_len(p, dst);
     const uint32_t nt = min(ntg_of(p, dst), t1);
-    for (uint32_t t = t0 + b; t < nt; t += G) {
+    for (uint32_t t = t0 + first; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
       const char* src = p.in + (s0 + (uint64_t)t * TG_ELEMS) * ES;
       char* slot = rs_slot(dst, me, t, ck);
-      if (p.hybrid) cta_copy_bytes(slot, src, tn * ES);
-      else encode_tg<DT>(src, tn, slot, sm.enc, LV);
+      if (p.hybrid) {
+        cta_copy_bytes(slot, src, tn * ES);
+      } else if (p.stage_local) {
+        // encode next to this CTA (the slot of my own slice's TG t on my heap,
+        // not yet used in this chunk), then push the record in 16-byte vectors
+        char* loc = ag_slot(c.heap[me], me, t, ck);
+        const uint32_t bytes = encode_tg<DT>(src, tn, loc, sm.enc, LV);
+        cta_push16(slot, loc, pad16(bytes));
+      } else {
+        encode_tg<DT>(src, tn, slot, sm.enc, LV);
+      }
       publish_block_writes(c);
       if (threadIdx.x == 0) st_release_sys(flag_of(slot), ready);
     }
@@ -338,7 +374,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
     const uint64_t s0 = slice_begin(p, me), sl = slice_len(p, me);
     const uint32_t nt = min(ntg_of(p, me), t1);
     float* acc = p.acc + (size_t)b * TG_ELEMS;
-    for (uint32_t t = t0 + b; t < nt; t += G) {
+    for (uint32_t t = t0 + first; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
       const uint64_t e0 = s0 + (uint64_t)t * TG_ELEMS;
       char* out_tg = p.out + e0 * ES;
@@ -388,11 +424,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
           multimem_st_release_u64(flag_of(mc), ready);
         }
       } else {
-        for (int k = 1; k < W; ++k) {
-          char* dstp = ag_slot(c.heap[(me + k) % W], me, t, ck);
-          for (uint32_t o = threadIdx.x * 16; o < padded; o += blockDim.x * 16)
-            st_v4(dstp + o, ld_cg_v4(mine + o));
-        }
+        for (int k = 1; k < W; ++k) cta_push16(ag_slot(c.heap[(me + k) % W], me, t, ck), mine, padded);
         publish_block_writes(c);
         if (threadIdx.x == 0)
           for (int k = 1; k < W; ++k) st_release_sys(flag_of(ag_slot(c.heap[(me + k) % W], me, t, ck)), ready);
@@ -406,7 +438,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
     const int own = (me + W - k) % W;
     const uint64_t s0 = slice_begin(p, own), sl = slice_len(p, own);
     const uint32_t nt = min(ntg_of(p, own), t1);
-    for (uint32_t t = t0 + b; t < nt; t += G) {
+    for (uint32_t t = t0 + first; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
       if (!wait_slot(ag_slot(c.heap[me], own, t, ck), 3, own)) return;
       if (p.use_mc) fence_proxy_alias();  // the record arrived through the multicast mapping
@@ -417,12 +449,11 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
       }
     }
   }
-  // chunk ck done on this CTA: peers may refill its ring slots with chunk
-  // ck + 2 (only progress that some peer waits for is published, so no write
-  // of this call is still in flight when the next call clears the row)
+  // chunk ck done on this CTA: every rank (this one included) may refill the
+  // ring slots it read or staged with chunk ck + 2
   if (ck + 2 < p.nchunks) {
     publish_block_writes(c);
-    if (threadIdx.x < (unsigned)W && (int)threadIdx.x != me) st_release_sys(prog(threadIdx.x, me), ck + 1);
+    if (threadIdx.x < (unsigned)W) st_release_sys(prog(threadIdx.x, b, me), done_value(ck));
   }
   }  // chunks
   epoch_advance(c);
@@ -490,8 +521,7 @@ static CzGeom cz_geom(size_t n, int world, size_t chunk_elems) {
 static size_t cz_stage_bytes(size_t n, int dtype, int world, int nblocks, size_t chunk_elems) {
   const CzGeom g = cz_geom(n, world, chunk_elems);
   const uint64_t sstride = tg_capacity(dtype) + 16;  // record capacity + flag footer
-  const size_t prog = (size_t)LZ_MAX_BLOCKS * LZ_MAX_RANKS * 8;
-  return 2 * (size_t)world * g.nslots * sstride + (size_t)nblocks * TG_ELEMS * 4 + prog + 256;
+  return 2 * (size_t)world * g.nslots * sstride + (size_t)nblocks * TG_ELEMS * 4 + 256;
 }
 
 // Bytes of the compressed-allreduce staging region for n elements (one chunk).
@@ -544,16 +574,18 @@ static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dty
   p.ag_off = c->stage_off + slots;
   const size_t acc_off = p.ag_off + slots;
   p.acc = reinterpret_cast<float*>(c->dev.heap[c->dev.rank] + acc_off);
-  p.prog_off = (acc_off + (size_t)G * TG_ELEMS * 4 + 15) / 16 * 16;
   p.use_mc = ((flags & 1) && c->dev.heap_mc) ? 1 : 0;
   p.hybrid = (flags & 2) ? 1 : 0;
+  p.stage_local = (flags & 8) ? 1 : 0;
   *out_p = p;
   return LZE_OK;
 }
 
 // flags: bit 0 multicast all-gather, bit 1 hybrid (raw reduce-scatter, the
 // compressed P2P hybrid of the reference's compressed_p2p_allreduce.py:54-188),
-// bit 2 PACK codec level. chunk_elems: see cz_geom (0: one chunk).
+// bit 2 PACK codec level, bit 3 encode reduce-scatter records locally and push
+// them as 16-byte vectors (instead of encoding straight into the peer's slot).
+// chunk_elems: see cz_geom (0: one chunk).
 extern "C" int lz_compressed_allreduce_chunked(LzComm* c, const void* in, void* out, size_t n, int dtype,
                                                int nblocks, int flags, size_t chunk_elems, cudaStream_t s) {
   const int W = c->dev.world;
@@ -598,7 +630,7 @@ extern "C" int lz_emu_compressed_allreduce_chunked(LzEmu* e, const void* const* 
   }
   CzParams hp[LZ_MAX_RANKS];
   for (int r = 0; r < R; ++r) {
-    int rc = cz_plan(lz_emu_comm(e, r), ins[r], outs[r], n, dtype, G, flags & 2, chunk_elems, &hp[r]);
+    int rc = cz_plan(lz_emu_comm(e, r), ins[r], outs[r], n, dtype, G, flags & (2 | 8), chunk_elems, &hp[r]);
     if (rc) return rc;
   }
   static_assert(sizeof(CzParams) * LZ_MAX_RANKS <= 4096, "param buffer");

@@ -35,6 +35,7 @@ int lz_heap_world(LzHeap* h);
 //   [480K, 480K+128) copy-engine ready / clear-to-send                  lz_weights.cu
 //   [512K]          failure-test flag that nothing sets                 lz_allreduce.cu
 //   [544K, 562K)    copy-engine two-shot: started / done / chunk flags   lz_copy_engine.cu
+//   [576K, 608K)    compressed allreduce chunk progress [block][rank]   lz_compressed.cu
 // (static_asserts next to each region keep neighbours from overlapping.)
 static constexpr size_t kLzFlagsBytes = 1 << 20;
 static constexpr size_t kLzLlMaxBytes = 256u << 10;  // largest low-latency one-shot message

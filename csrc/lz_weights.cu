@@ -49,6 +49,7 @@ struct WxParams {
   int use_mc;
   int kslots;
   int group;         // table groups per work item (one flag round trip per item)
+  int stage_local;   // encode records locally and push them, even to a single receiver
   uint32_t cap;
   size_t slots_off;
   size_t ready_off;
@@ -178,7 +179,9 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
         char* local = c.heap[me] + slot_off;
         const int es = es_of(d.dtype);
         if (d.encode) {
-          const bool direct = !p.use_mc && nrecv == 1;
+          // one receiver: encode straight into its slot, unless the records are
+          // staged locally and pushed as 16-byte vectors (p.stage_local)
+          const bool direct = !p.use_mc && nrecv == 1 && !p.stage_local;
           char* dst = direct ? c.heap[only] + slot_off : local;
           if (!lz_range_ok(c, dst, p.cap, 21)) return;
           const uint32_t bytes = encode_dispatch(d.dtype, d.ptr, d.n, dst, sm.enc, d.encode);
@@ -311,6 +314,12 @@ static int wx_plan(const LzComm* c, int role, int src, unsigned int recv_mask, c
   p.cap = tg_capacity(LZ_F32);
   p.slots_off = c->stage_off;
   p.group = wx_group();
+  {
+    // diagnostic: LZ_WX_STAGE_LOCAL=1 encodes a single receiver's records
+    // locally and pushes them as vectors instead of encoding into its slot
+    static const char* e = getenv("LZ_WX_STAGE_LOCAL");
+    p.stage_local = e ? atoi(e) : 0;
+  }
   if (lz_wx_stage_bytes(G, kslots) * p.group > c->stage_bytes) {
     lz_set_error("weight transfer: %d blocks x %d slots x %d groups need %zu stage bytes, have %zu", G,
                  kslots, p.group, lz_wx_stage_bytes(G, kslots) * p.group, c->stage_bytes);

@@ -63,7 +63,8 @@ def main(argv=None):
     ap.add_argument("--variants", default="compressed,hybrid,compressed_pack,hybrid_pack",
                     help="compressed: reduce-scatter and all-gather compressed; hybrid: raw reduce-scatter, "
                          "compressed all-gather; the _pack suffix codes records with the codec's PACK "
-                         "level (table codes) instead of rANS")
+                         "level (table codes) instead of rANS; a trailing _local encodes reduce-scatter "
+                         "records locally and pushes them")
     ap.add_argument("--fp8", action="store_true", default=True)
     ap.add_argument("--no-fp8", dest="fp8", action="store_false")
     ap.add_argument("--iters", type=int, default=5)
@@ -136,12 +137,12 @@ def main(argv=None):
                 for cmb, var in [(cm, vv) for cm in chunks for vv in a.variants.split(",")]:
                     if cmb and cmb * MiB >= nbytes:
                         continue
-                    level = "pack" if var.endswith("_pack") else "ans"
+                    level = "pack" if "_pack" in var else "ans"
                     ratio = ratios[level]
 
-                    def run(hybrid=var.startswith("hybrid"), level=level, cb=cmb * MiB):
+                    def run(hybrid=var.startswith("hybrid"), level=level, cb=cmb * MiB, loc=var.endswith("_local")):
                         cz.compressed_allreduce(x, y, comm=comm, nblocks=nb, hybrid=hybrid, level=level,
-                                                chunk_bytes=cb)
+                                                chunk_bytes=cb, stage_local=loc)
 
                     torch.cuda.reset_peak_memory_stats()
                     m0 = torch.cuda.memory_allocated()

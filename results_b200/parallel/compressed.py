@@ -66,7 +66,8 @@ def stage_bytes_needed(n: int, dtype: torch.dtype, world: int, nblocks: int = 44
 @traced("compressed_allreduce")
 def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=None,
                          nblocks: int = 0, multicast: bool = True, stream=None,
-                         hybrid: bool = False, level="ans", chunk_bytes: int = 0) -> torch.Tensor:
+                         hybrid: bool = False, level="ans", chunk_bytes: int = 0,
+                         stage_local: bool = False) -> torch.Tensor:
     """Sum-allreduce with lossless compression on the wire (native fused kernel).
 
     ``level``: codec level of the records, "ans" (rANS, best ratio) or "pack"
@@ -78,6 +79,9 @@ def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=
     two chunks' slots, so the stage memory is bounded by the chunk size while
     encoding, transfer and decoding of neighbouring chunks overlap (a CTA
     starts chunk k + 2 as soon as every rank's same CTA has finished chunk k).
+    ``stage_local`` encodes reduce-scatter records next to the encoding CTA
+    and pushes them to the peer in 16-byte vectors instead of encoding
+    straight into the peer's slot.
 
     ``hybrid=True`` is the compressed P2P hybrid: the reduce-scatter moves raw
     bytes and only the all-gather of the reduced slices is compressed, so each
@@ -97,7 +101,7 @@ def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=
     rc = comm._lib.lz_compressed_allreduce_chunked(comm.handle, t.data_ptr(), out.data_ptr(), t.numel(),
                                                    lz_dtype(t.dtype), nb,
                                                    int(multicast) | (2 if hybrid else 0) |
-                                                   (4 * codec.level_code(level)),
+                                                   (4 * codec.level_code(level)) | (8 if stage_local else 0),
                                                    chunk_elems, s.cuda_stream)
     _native.check(rc, "compressed_allreduce")
     return out
@@ -240,60 +244,86 @@ def compressed_twoshot(t: torch.Tensor, group=None, ratio: float = 0.65) -> torc
     return t
 
 
-def compressed_ring(t: torch.Tensor, group=None, ratio: float = 0.65) -> torch.Tensor:
-    """Ring RS + AG over compressed chunks (bf16 partial sums per hop, as NCCL)."""
+def compressed_ring(t: torch.Tensor, group=None, ratio: float = 0.65, pieces: int = 2) -> torch.Tensor:
+    """Ring RS + AG over compressed chunks (bf16 partial sums per hop, as NCCL).
+
+    Double-buffered: every ring chunk travels as ``pieces`` pieces whose
+    fixed-budget messages are posted asynchronously (isend/irecv), so piece
+    k + 1 is encoded while piece k is on the wire; received pieces are decoded
+    after the posts. The all-gather forwards the compressed stream it received
+    instead of re-encoding it. The reference overlaps compression of the next
+    chunk with the current transfer in the same way
+    (single_node_nccl_allreduce_benchmark/compressed_sendrecv_allreduce.py:41-231).
+    """
     rank, ws, gr = _info(group)
     if ws == 1:
         return t
     ch = _chunks(t, ws)
     right, left = gr[(rank + 1) % ws], gr[(rank - 1) % ws]
-    budget = budget_bytes(max(c.numel() for c in ch), t.element_size(), ratio)
+    P = max(1, int(pieces))
+
+    def parts(x):  # P contiguous pieces of a chunk view
+        n = x.numel()
+        return [x[(n * k) // P:(n * (k + 1)) // P] for k in range(P)]
+
+    pbudget = budget_bytes(max(c.numel() for c in ch) // P + 1, t.element_size(), ratio)
+
+    def hop(send_blobs, recv_shapes, encode_next=None):
+        """One ring step: post every piece's message (encoding the next piece
+        while the previous one is in flight), then finish overflows and return
+        the received streams (compressed, per piece)."""
+        posted = []
+        blob = send_blobs(0)
+        for k in range(P):
+            msg, rest = _pack(blob, pbudget)
+            r = torch.empty(pbudget, dtype=torch.uint8, device=t.device)
+            works = dist.batch_isend_irecv([dist.P2POp(dist.isend, msg, right, group=group),
+                                            dist.P2POp(dist.irecv, r, left, group=group)])
+            STATS.sent_bytes += min(blob.numel(), pbudget - HDR) + HDR
+            posted.append((works, msg, r, rest))
+            if k + 1 < P:
+                blob = send_blobs(k + 1)  # overlaps the transfer of piece k
+        streams = []
+        for works, msg, r, rest in posted:
+            for w in works:
+                w.wait()
+            size, over = _unpack_header(r)
+            ops, tail = [], None
+            if rest is not None:
+                ops.append(dist.P2POp(dist.isend, rest, right, group=group))
+                STATS.sent_bytes += rest.numel()
+                STATS.overflows += 1
+            if over:
+                tail = torch.empty(size - (pbudget - HDR), dtype=torch.uint8, device=r.device)
+                ops.append(dist.P2POp(dist.irecv, tail, left, group=group))
+            if ops:
+                for w in dist.batch_isend_irecv(ops):
+                    w.wait()
+            stream = r[HDR:HDR + min(size, pbudget - HDR)]
+            streams.append(torch.cat([stream, tail]) if tail is not None else stream.contiguous())
+        return streams
+
+    # reduce-scatter: send my partial sum of chunk si, add the received one into chunk ri
     si, ri = rank, (rank - 1) % ws
-    nxt = _encode(ch[si].contiguous())
-    for step in range(ws - 1):
-        cur = nxt
-        # exchange with both neighbours: send right, receive from left
-        got = _ring_hop(cur, right, left, group, budget, ch[ri].numel(), t.dtype)
-        ch[ri].add_(got.view(ch[ri].shape))
+    for _ in range(ws - 1):
+        src_parts, dst_parts = parts(ch[si]), parts(ch[ri])
+        got = hop(lambda k, sp=src_parts: _encode(sp[k].contiguous()), None)
+        for k, g in enumerate(got):
+            dst_parts[k].add_(_decode(g, dst_parts[k].numel(), t.dtype).view(dst_parts[k].shape))
         STATS.raw_bytes += ch[si].numel() * t.element_size()
         si, ri = ri, (ri - 1) % ws
-        nxt = _encode(ch[si].contiguous())
+    # all-gather: encode my reduced chunk once, then forward what arrives
     si, ri = (rank + 1) % ws, rank
-    nxt = _encode(ch[si].contiguous())
-    for step in range(ws - 1):
-        got = _ring_hop(nxt, right, left, group, budget, ch[ri].numel(), t.dtype)
-        ch[ri].copy_(got.view(ch[ri].shape))
+    fwd = [_encode(x.contiguous()) for x in parts(ch[si])]
+    for _ in range(ws - 1):
+        got = hop(lambda k, f=fwd: f[k], None)
+        dst_parts = parts(ch[ri])
+        for k, g in enumerate(got):
+            dst_parts[k].copy_(_decode(g, dst_parts[k].numel(), t.dtype).view(dst_parts[k].shape))
         STATS.raw_bytes += ch[si].numel() * t.element_size()
+        fwd = got
         si, ri = ri, (ri - 1) % ws
-        nxt = _encode(ch[si].contiguous()) if step < ws - 2 else None
     return t
-
-
-@traced("ring_hop")
-def _ring_hop(blob, right, left, group, budget, n_recv, dtype):
-    msg, rest = _pack(blob, budget)
-    r = torch.empty(budget, dtype=torch.uint8, device=blob.device)
-    for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, msg, right, group=group),
-                                     dist.P2POp(dist.irecv, r, left, group=group)]):
-        w.wait()
-    STATS.sent_bytes += min(blob.numel(), budget - HDR) + HDR
-    size, over = _unpack_header(r)
-    ops = []
-    tail = None
-    if rest is not None:
-        ops.append(dist.P2POp(dist.isend, rest, right, group=group))
-        STATS.sent_bytes += rest.numel()
-        STATS.overflows += 1
-    if over:
-        tail = torch.empty(size - (budget - HDR), dtype=torch.uint8, device=r.device)
-        ops.append(dist.P2POp(dist.irecv, tail, left, group=group))
-    if ops:
-        for w in dist.batch_isend_irecv(ops):
-            w.wait()
-    stream = r[HDR:HDR + min(size, budget - HDR)]
-    if tail is not None:
-        stream = torch.cat([stream, tail])
-    return _decode(stream.contiguous(), n_recv, dtype)
 
 
 def compressed_nosize(t: torch.Tensor, group=None, ratio: float = 0.65) -> torch.Tensor:

@@ -74,13 +74,13 @@ def test_compressed_inplace_activation_like(worlds, level):
 @pytest.mark.parametrize("level", ["ans", "pack"])
 @pytest.mark.parametrize("hybrid", [False, True])
 @pytest.mark.parametrize("R", [2, 4])
-@pytest.mark.parametrize("chunk_tgs,nblocks", [(1, 3), (2, 8), (3, 2)])
+@pytest.mark.parametrize("chunk_tgs,nblocks", [(1, 1), (2, 2), (3, 2), (5, 3)])
 def test_compressed_allreduce_chunked_ring(worlds, R, hybrid, level, chunk_tgs, nblocks):
-    """In-launch chunks through a ring of two chunks' slots: slices of 6+ table
-    groups in chunks of 1-3 TGs, CTAs fewer or more than a chunk's TGs, three
+    """In-launch chunks through a ring of two chunks' slots: slices of 13 table
+    groups in chunks of 1-6 TGs (rounded up to the grid), 3 to 13 chunks, three
     calls in a row (progress flags are cleared per call), bit-exact."""
     w = worlds[R]
-    n = 32768 * R * 6 + 48 * R + 16
+    n = 32768 * R * 12 + 48 * R + 16
     outs = None
     for it in range(3):
         xs = _inputs(R, n, torch.bfloat16, seed=1000 * it + 10 * R + chunk_tgs)
@@ -104,3 +104,26 @@ def test_chunked_stage_is_bounded():
     whole = cz.stage_bytes_needed(n, torch.bfloat16, 8, 444)
     chunked = cz.stage_bytes_needed(n, torch.bfloat16, 8, 444, chunk_elems=(64 << 20) // 2)
     assert chunked < whole / 3
+
+
+@pytest.mark.parametrize("level", ["ans", "pack"])
+@pytest.mark.parametrize("R", [2, 4])
+@pytest.mark.parametrize("chunk", [0, 2])
+def test_compressed_allreduce_stage_local(worlds, R, level, chunk):
+    """Reduce-scatter records encoded locally and pushed as vectors, with and
+    without chunks: same bit-exact result."""
+    w = worlds[R]
+    n = 32768 * R * 7 + 1000
+    xs = _inputs(R, n, torch.float16, seed=77 + R)
+    outs = [torch.empty_like(x) for x in xs]
+    for _ in range(2):
+        w.compressed_allreduce(xs, outs, nblocks=4, level=level, chunk_elems=32768 * R * chunk,
+                               stage_local=True)
+    torch.cuda.synchronize()
+    acc = xs[0].float().clone()
+    for x in xs[1:]:
+        acc += x.float()
+    ref = acc.to(torch.float16)
+    for r in range(R):
+        assert w.status(r) == 0
+        assert torch.equal(outs[r], ref), r
