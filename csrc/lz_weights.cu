@@ -96,28 +96,23 @@ LZ_DEV void push_bytes(const LzDevComm& c, char* dst, const char* src, uint32_t 
   }
 }
 
-template <int DT>
-LZ_DEV uint32_t encode_any(const char* in, uint32_t n, char* dst, EncSmem& sm, int level) {
-  return level == LEVEL_PACK ? encode_tg<DT>(in, n, dst, sm, LEVEL_PACK)
-                             : encode_tg<DT>(in, n, dst, sm, LEVEL_ANS);
-}
-
-// `enc`: descriptor encode field (1 ANS, 2 PACK)
-LZ_DEV uint32_t encode_dispatch(int dt, const char* in, uint32_t n, char* dst, EncSmem& sm, int enc) {
-  const int level = enc == 2 ? LEVEL_PACK : LEVEL_ANS;
+// Records are encoded at the kernel's level LV (one instantiation per level,
+// chosen by the host from the engine's mode).
+template <int LV>
+LZ_DEV uint32_t encode_dispatch(int dt, const char* in, uint32_t n, char* dst, EncSmem& sm) {
   switch (dt) {
     case LZ_F32:
-      return encode_any<DT_F32>(in, n, dst, sm, level);
+      return encode_tg<DT_F32>(in, n, dst, sm, LV);
     case LZ_F16:
-      return encode_any<DT_F16>(in, n, dst, sm, level);
+      return encode_tg<DT_F16>(in, n, dst, sm, LV);
     case LZ_BF16:
-      return encode_any<DT_BF16>(in, n, dst, sm, level);
+      return encode_tg<DT_BF16>(in, n, dst, sm, LV);
     case DT_E4M3P:
-      return encode_any<DT_E4M3P>(in, n, dst, sm, level);
+      return encode_tg<DT_E4M3P>(in, n, dst, sm, LV);
     case DT_E5M2P:
-      return encode_any<DT_E5M2P>(in, n, dst, sm, level);
+      return encode_tg<DT_E5M2P>(in, n, dst, sm, LV);
     default:
-      return encode_any<DT_U8>(in, n, dst, sm, level);
+      return encode_tg<DT_U8>(in, n, dst, sm, LV);
   }
 }
 
@@ -138,6 +133,7 @@ LZ_DEV bool decode_dispatch(int dt, const char* rec, uint32_t cap, uint32_t n, c
   }
 }
 
+template <int LV>
 __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
   extern __shared__ __align__(16) char smem_raw[];
   WxSmem& sm = *reinterpret_cast<WxSmem*>(smem_raw);
@@ -184,7 +180,7 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
           const bool direct = !p.use_mc && nrecv == 1 && !p.stage_local;
           char* dst = direct ? c.heap[only] + slot_off : local;
           if (!lz_range_ok(c, dst, p.cap, 21)) return;
-          const uint32_t bytes = encode_dispatch(d.dtype, d.ptr, d.n, dst, sm.enc, d.encode);
+          const uint32_t bytes = encode_dispatch<LV>(d.dtype, d.ptr, d.n, dst, sm.enc);
           if (p.use_mc) {
             push_bytes<true>(c, c.heap_mc + slot_off, local, pad16(bytes));
           } else if (!direct) {
@@ -266,7 +262,14 @@ __device__ __forceinline__ void wx_body(const LzDevComm& c, const WxParams& p) {
   }
 }
 
-__global__ void __launch_bounds__(LZC_THREADS, 2) wx_kernel(LzDevComm c, WxParams p) { wx_body(c, p); }
+template <int LV>
+__global__ void __launch_bounds__(LZC_THREADS, LZC_MIN_BLOCKS) wx_kernel(LzDevComm c, WxParams p) {
+  wx_body<LV>(c, p);
+}
+// flags bit 1: records at the PACK level
+void* wx_fn(int flags) {
+  return (flags & 2) ? reinterpret_cast<void*>(&wx_kernel<LEVEL_PACK>) : reinterpret_cast<void*>(&wx_kernel<LEVEL_ANS>);
+}
 
 }  // namespace
 
@@ -307,7 +310,7 @@ static int wx_plan(const LzComm* c, int role, int src, unsigned int recv_mask, c
   p.role = role;
   p.src = src;
   p.recv_mask = recv_mask;
-  const bool all = broadcast_all && recv_mask == (((1u << W) - 1u) & ~(1u << src));
+  const bool all = (broadcast_all & 1) && recv_mask == (((1u << W) - 1u) & ~(1u << src));
   // one receiver: direct peer stores beat a multicast write that also lands locally
   p.use_mc = (all && W > 2 && c->dev.heap_mc) ? 1 : 0;
   p.kslots = kslots;
@@ -333,6 +336,8 @@ static int wx_plan(const LzComm* c, int role, int src, unsigned int recv_mask, c
   return LZE_OK;
 }
 
+// broadcast_all: bit 0 every rank but src receives (multicast when possible),
+// bit 1 encoded records use the codec's PACK level (else rANS).
 extern "C" int lz_weight_transfer(LzComm* c, int role, int src, unsigned int recv_mask,
                                   const void* descs, unsigned int ntg, int nblocks, int kslots,
                                   int broadcast_all, const unsigned long long* seqs, cudaStream_t s) {
@@ -342,7 +347,7 @@ extern "C" int lz_weight_transfer(LzComm* c, int role, int src, unsigned int rec
   int rc = wx_plan(c, role, src, recv_mask, descs, ntg, nblocks, kslots, broadcast_all, seqs, &p, &G);
   if (rc) return rc;
   const size_t smem = sizeof(WxSmem);
-  void* fn = reinterpret_cast<void*>(&wx_kernel);
+  void* fn = wx_fn(broadcast_all);
   LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* args[] = {&c->dev, &p};
   LZ_CUDA_TRY(cudaLaunchKernel(fn, dim3(G), dim3(LZC_THREADS), args, smem, s));
@@ -353,10 +358,11 @@ extern "C" int lz_weight_transfer(LzComm* c, int role, int src, unsigned int rec
 // rank y, all in ONE cooperative launch; ranks that neither send nor receive
 // idle. descs[r]: device descriptor table of rank r; seqs: R x 8 values.
 namespace {
+template <int LV>
 __global__ void __launch_bounds__(LZC_THREADS, 2) wx_emu_kernel(const LzDevComm* cs, const WxParams* ps) {
   const WxParams& p = ps[blockIdx.y];
   if (p.role > 1) return;
-  wx_body(cs[blockIdx.y], p);
+  wx_body<LV>(cs[blockIdx.y], p);
 }
 }  // namespace
 
@@ -374,7 +380,8 @@ extern "C" int lz_emu_weight_transfer(LzEmu* e, int src, unsigned int recv_mask,
     hp[r].role = role;
   }
   const size_t smem = sizeof(WxSmem);
-  void* fn = reinterpret_cast<void*>(&wx_emu_kernel);
+  void* fn = (broadcast_all & 2) ? reinterpret_cast<void*>(&wx_emu_kernel<LEVEL_PACK>)
+                                 : reinterpret_cast<void*>(&wx_emu_kernel<LEVEL_ANS>);
   LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
   LZ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, LZC_THREADS, smem));

@@ -112,8 +112,9 @@ class EmulatedWorld:
             ntg = n
         arr = (C.c_void_p * R)(*ptrs)
         sq = (C.c_uint64 * (8 * R))(*seqs)
+        flags = int(broadcast_all) | (2 if encode == 2 else 0)  # bit 1: PACK-level records
         rc = self._lib.lz_emu_weight_transfer(self._emu, src, mask, arr, ntg, nblocks, kslots,
-                                              int(broadcast_all), sq, torch.cuda.current_stream().cuda_stream)
+                                              flags, sq, torch.cuda.current_stream().cuda_stream)
         _native.check(rc, "emulated weight transfer")
 
     def all_to_all(self, ins, outs, compress: bool = False, nblocks: int = 0):

@@ -134,8 +134,10 @@ class WeightTransfer:
     def _launch(self, role, src, mask, descs, ntg, all_, seqs):
         arr = (C.c_uint64 * 8)(*seqs)
         s = torch.cuda.current_stream(self.comm.device)
+        # flags: bit 0 every other rank receives, bit 1 records at the codec's PACK level
+        flags = int(all_) | (2 if self.mode == "split_pack" else 0)
         rc = self.comm._lib.lz_weight_transfer(self.comm.handle, role, src, mask, descs.data_ptr(), ntg,
-                                               self.nblocks, self.kslots, int(all_), arr, s.cuda_stream)
+                                               self.nblocks, self.kslots, flags, arr, s.cuda_stream)
         _native.check(rc, "weight transfer")
 
     def _flags(self, tensors):
