@@ -64,9 +64,28 @@ struct CzParams {
   int use_mc;          // publish AG records with multimem.st
   int hybrid;          // reduce-scatter moves raw bytes; only the all-gather is compressed
   int stage_local;     // RS records are encoded into local memory, then pushed as 16-byte vectors
+  unsigned long long* trace;  // optional: per-CTA nanoseconds per phase [G][kCzTraceSlots]
   uint32_t chunk_tgs;  // TGs per slice per chunk (C); every slice is processed in chunks of C TGs
   uint32_t nchunks;    // ceil(ntg_max / C)
   uint32_t nslots;     // slots per source: ntg_max (one chunk) or 2 C (a ring of two chunks)
+};
+
+// Phase tracer: with a trace buffer, thread 0 of every CTA adds the
+// %globaltimer nanoseconds spent in each phase to its row (added across calls).
+enum CzPhase {
+  CZ_T_TOTAL = 0,    // kernel start to end of the CTA
+  CZ_T_BARRIER,      // start barrier
+  CZ_T_RS_ENCODE,    // reduce-scatter: encode (or copy) + push of records to peers
+  CZ_T_RS_WAIT,      // owner: waiting for peers' records
+  CZ_T_RS_DECODE,    // owner: decoding records' symbols
+  CZ_T_REDUCE,       // owner: rank-order fp32 reduction passes
+  CZ_T_AG_ENCODE,    // owner: encoding the reduced table group
+  CZ_T_AG_PUSH,      // owner: publishing it (peer stores or multimem) + flags
+  CZ_T_AG_WAIT,      // waiting for the other owners' records
+  CZ_T_AG_DECODE,    // decoding them into the output
+  CZ_T_CHUNK_WAIT,   // waiting for ring slots (chunked calls)
+  CZ_T_TGS,          // table groups reduced by this CTA (a count)
+  kCzTraceSlots = 12
 };
 
 // Chunk progress words [LZ_MAX_BLOCKS][LZ_MAX_RANKS] in the flag area (a
@@ -321,8 +340,24 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
     __syncthreads();
     return s_wfail == 0;
   };
+  // phase tracer: thread 0 keeps the running sums in shared memory
+  // (s_tr[kCzTraceSlots] = last mark, s_tr[kCzTraceSlots + 1] = start)
+  __shared__ unsigned long long s_tr[kCzTraceSlots + 2];
+  const bool tr = p.trace != nullptr && threadIdx.x == 0;
+  if (tr) {
+    for (int k = 0; k < kCzTraceSlots; ++k) s_tr[k] = 0ull;
+    s_tr[kCzTraceSlots] = s_tr[kCzTraceSlots + 1] = globaltimer();
+  }
+  auto lap = [&](int slot) {  // time since the last mark goes to `slot`
+    if (tr) {
+      const unsigned long long now = globaltimer();
+      s_tr[slot] += now - s_tr[kCzTraceSlots];
+      s_tr[kCzTraceSlots] = now;
+    }
+  };
   // every rank's CTA b has finished the previous call
   if (!block_barrier(c, epoch, 1)) return;
+  lap(CZ_T_BARRIER);
 
   for (uint32_t ck = 0; ck < p.nchunks; ++ck) {
   ready = ready_of(ck);
@@ -342,6 +377,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
     __syncthreads();
     if (s_pfail) return;
   }
+  lap(CZ_T_CHUNK_WAIT);
 
   // 1. encode my input's TGs of every peer's slice into that peer's RS slots
   //    (hybrid: copy them raw; the reduce-scatter then pays no codec work)
@@ -368,6 +404,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
       if (threadIdx.x == 0) st_release_sys(flag_of(slot), ready);
     }
   }
+  lap(CZ_T_RS_ENCODE);
 
   // 2. decode + reduce (rank order, fp32) + store + re-encode + publish
   {
@@ -392,6 +429,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
             return true;
           }
           if (!wait_slot(rs_slot(me, r, t, ck), 2, r)) return false;
+          lap(CZ_T_RS_WAIT);
           const char* rec = rs_slot(me, r, t, ck);
           if (p.hybrid) {
             out_src = RedSrc{rec, nullptr};
@@ -401,6 +439,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
             if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 2, r);
             return false;
           }
+          lap(CZ_T_RS_DECODE);
           out_src = RedSrc{nullptr, rec + sizeof(TgHeader)};
           return true;
         };
@@ -409,10 +448,12 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
         if (pair && !source(1, b2)) return;
         reduce_pass<DT>(a, pair ? &b2 : nullptr, sm.dec, tn, acc, s == 0, last == W - 1 ? out_tg : nullptr);
         __syncthreads();
+        lap(CZ_T_REDUCE);
         s = last + 1;
       }
       char* mine = ag_slot(c.heap[me], me, t, ck);
       const uint32_t bytes = encode_tg<DT>(p.out + e0 * ES, tn, mine, sm.enc, LV);
+      lap(CZ_T_AG_ENCODE);
       const uint32_t padded = pad16(bytes);
       if (p.use_mc) {
         char* mc = ag_slot(c.heap_mc, me, t, ck);
@@ -430,6 +471,8 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
           for (int k = 1; k < W; ++k) st_release_sys(flag_of(ag_slot(c.heap[(me + k) % W], me, t, ck)), ready);
       }
       __syncthreads();
+      lap(CZ_T_AG_PUSH);
+      if (tr) s_tr[CZ_T_TGS] += 1;
     }
   }
 
@@ -441,12 +484,14 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
     for (uint32_t t = t0 + first; t < nt; t += G) {
       const uint32_t tn = (uint32_t)min((uint64_t)TG_ELEMS, sl - (uint64_t)t * TG_ELEMS);
       if (!wait_slot(ag_slot(c.heap[me], own, t, ck), 3, own)) return;
+      lap(CZ_T_AG_WAIT);
       if (p.use_mc) fence_proxy_alias();  // the record arrived through the multicast mapping
       if (!decode_tg<DT>(ag_slot(c.heap[me], own, t, ck), p.cap, tn, p.out + (s0 + (uint64_t)t * TG_ELEMS) * ES,
                          sm.dec)) {
         if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 3, own);
         return;
       }
+      lap(CZ_T_AG_DECODE);
     }
   }
   // chunk ck done on this CTA: every rank (this one included) may refill the
@@ -455,7 +500,13 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
     publish_block_writes(c);
     if (threadIdx.x < (unsigned)W) st_release_sys(prog(threadIdx.x, b, me), done_value(ck));
   }
+  lap(CZ_T_CHUNK_WAIT);
   }  // chunks
+  if (tr) {
+    s_tr[CZ_T_TOTAL] = globaltimer() - s_tr[kCzTraceSlots + 1];
+    unsigned long long* row = p.trace + (size_t)b * kCzTraceSlots;
+    for (int k = 0; k < kCzTraceSlots; ++k) row[k] += s_tr[k];
+  }
   epoch_advance(c);
 }
 
@@ -525,6 +576,8 @@ static size_t cz_stage_bytes(size_t n, int dtype, int world, int nblocks, size_t
 }
 
 // Bytes of the compressed-allreduce staging region for n elements (one chunk).
+extern "C" int lz_cz_trace_slots(void) { return kCzTraceSlots; }
+
 extern "C" size_t lz_cz_stage_bytes(size_t n, int dtype, int world, int nblocks) {
   return cz_stage_bytes(n, dtype, world, nblocks, 0);
 }
@@ -586,8 +639,19 @@ static int cz_plan(const LzComm* c, const void* in, void* out, size_t n, int dty
 // bit 2 PACK codec level, bit 3 encode reduce-scatter records locally and push
 // them as 16-byte vectors (instead of encoding straight into the peer's slot).
 // chunk_elems: see cz_geom (0: one chunk).
+// trace: optional device buffer of nblocks x lz_cz_trace_slots() u64 (phase
+// nanoseconds per CTA, added to; phases in CzPhase), or nullptr.
+extern "C" int lz_compressed_allreduce_traced(LzComm* c, const void* in, void* out, size_t n, int dtype,
+                                              int nblocks, int flags, size_t chunk_elems,
+                                              unsigned long long* trace, cudaStream_t s);
 extern "C" int lz_compressed_allreduce_chunked(LzComm* c, const void* in, void* out, size_t n, int dtype,
                                                int nblocks, int flags, size_t chunk_elems, cudaStream_t s) {
+  return lz_compressed_allreduce_traced(c, in, out, n, dtype, nblocks, flags, chunk_elems, nullptr, s);
+}
+
+extern "C" int lz_compressed_allreduce_traced(LzComm* c, const void* in, void* out, size_t n, int dtype,
+                                              int nblocks, int flags, size_t chunk_elems,
+                                              unsigned long long* trace, cudaStream_t s) {
   const int W = c->dev.world;
   const size_t es = dtype == LZ_F32 ? 4 : 2;
   if (W == 1) {
@@ -599,6 +663,7 @@ extern "C" int lz_compressed_allreduce_chunked(LzComm* c, const void* in, void* 
   CzParams p;
   int rc = cz_plan(c, in, out, n, dtype, G, flags, chunk_elems, &p);
   if (rc) return rc;
+  p.trace = trace;
   void* fn = cz_kernel_for(dtype, false, flags);
   const size_t smem = sizeof(CzSmem);
   LZ_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -613,9 +678,22 @@ extern "C" int lz_compressed_allreduce(LzComm* c, const void* in, void* out, siz
 }
 
 // Single-GPU emulation of the compressed allreduce over the R emulated ranks.
+// trace: optional device buffer of R x G x lz_cz_trace_slots() u64 (rank r's
+// CTA rows at r * G), or nullptr.
+extern "C" int lz_emu_compressed_allreduce_traced(LzEmu* e, const void* const* ins, void* const* outs,
+                                                  size_t n, int dtype, int nblocks, int flags,
+                                                  size_t chunk_elems, unsigned long long* trace,
+                                                  cudaStream_t s);
 extern "C" int lz_emu_compressed_allreduce_chunked(LzEmu* e, const void* const* ins, void* const* outs,
                                                    size_t n, int dtype, int nblocks, int flags,
                                                    size_t chunk_elems, cudaStream_t s) {
+  return lz_emu_compressed_allreduce_traced(e, ins, outs, n, dtype, nblocks, flags, chunk_elems, nullptr, s);
+}
+
+extern "C" int lz_emu_compressed_allreduce_traced(LzEmu* e, const void* const* ins, void* const* outs,
+                                                  size_t n, int dtype, int nblocks, int flags,
+                                                  size_t chunk_elems, unsigned long long* trace,
+                                                  cudaStream_t s) {
   const int R = lz_emu_world(e);
   void* fn = cz_kernel_for(dtype, true, flags);
   const size_t smem = sizeof(CzSmem);
@@ -632,6 +710,7 @@ extern "C" int lz_emu_compressed_allreduce_chunked(LzEmu* e, const void* const* 
   for (int r = 0; r < R; ++r) {
     int rc = cz_plan(lz_emu_comm(e, r), ins[r], outs[r], n, dtype, G, flags & (2 | 8), chunk_elems, &hp[r]);
     if (rc) return rc;
+    hp[r].trace = trace ? trace + (size_t)r * G * kCzTraceSlots : nullptr;
   }
   static_assert(sizeof(CzParams) * LZ_MAX_RANKS <= 4096, "param buffer");
   void* dparams = lz_emu_param_buffer(e);

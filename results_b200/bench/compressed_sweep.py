@@ -67,6 +67,9 @@ def main(argv=None):
                          "records locally and pushes them")
     ap.add_argument("--fp8", action="store_true", default=True)
     ap.add_argument("--no-fp8", dest="fp8", action="store_false")
+    ap.add_argument("--trace", action="store_true",
+                    help="after timing, run the call again with the kernel's per-CTA phase tracer and print "
+                         "the mean microseconds per phase (rank 0)")
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--csv", default=None)
@@ -149,6 +152,19 @@ def main(argv=None):
                     ms = timed(run, st)
                     extra = cz.stage_bytes_needed(n, torch.bfloat16, world, nb, chunk_elems=cmb * MiB // 2) + \
                         (torch.cuda.max_memory_allocated() - m0)
+                    if a.trace:
+                        tbuf = cz.trace_buffer(comm, nb)
+                        ctx = torch.cuda.stream(st.stream) if st is not None else torch.cuda.stream(
+                            torch.cuda.current_stream())
+                        with ctx:
+                            for _ in range(a.iters):
+                                cz.compressed_allreduce(x, y, comm=comm, nblocks=nb, hybrid=var.startswith("hybrid"),
+                                                        level=level, chunk_bytes=cmb * MiB,
+                                                        stage_local=var.endswith("_local"), trace=tbuf)
+                        torch.cuda.synchronize()
+                        if rank == 0:
+                            print(f"trace {kind} {csvfmt.size_label(nbytes)} sm={b or sms} chunk={cmb}MB {var}: "
+                                  f"{cz.summarize_trace(tbuf, a.iters)}", flush=True)
                     exact = bool(torch.equal(y, ref))
                     rows.append({**base, "sm_budget": b or sms, "chunk_mb": cmb, "variant": var,
                                  "ms": round(ms, 4), "algbw_GBps": round(nbytes / ms / 1e6, 2),

@@ -46,6 +46,12 @@ _native_sigs.add_cuda({
     "lz_emu_compressed_allreduce": (C.c_int, C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                     C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_void_p),
     "lz_cz_stage_bytes_chunked": (C.c_size_t, C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_size_t),
+    "lz_cz_trace_slots": (C.c_int,),
+    "lz_emu_compressed_allreduce_traced": (C.c_int, C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                           C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p,
+                                           C.c_void_p),
+    "lz_compressed_allreduce_traced": (C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
+                                       C.c_int, C.c_int, C.c_size_t, C.c_void_p, C.c_void_p),
     "lz_compressed_allreduce_chunked": (C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
                                         C.c_int, C.c_int, C.c_size_t, C.c_void_p),
     "lz_emu_compressed_allreduce_chunked": (C.c_int, C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
@@ -56,6 +62,29 @@ HDR = 16  # u64 stream size + u64 overflow flag
 
 
 # ----------------------------------------------------------------------------- native
+# Phases of the per-CTA tracer of the native kernel (csrc/lz_compressed.cu CzPhase).
+TRACE_PHASES = ("total", "start_barrier", "rs_encode_push", "rs_wait", "rs_decode", "reduce", "ag_encode",
+                "ag_push", "ag_wait", "ag_decode", "chunk_wait", "tgs_reduced")
+
+
+def trace_buffer(comm=None, nblocks: int = 0) -> torch.Tensor:
+    """Zeroed tracer rows (int64, one per CTA) for compressed_allreduce(trace=)."""
+    from .allreduce import get_comm
+
+    comm = comm or get_comm()
+    g = nblocks or comm.config.sm_budget or comm._lib.lz_cz_default_blocks(comm.handle)
+    assert comm._lib.lz_cz_trace_slots() == len(TRACE_PHASES)
+    return torch.zeros((g, len(TRACE_PHASES)), dtype=torch.int64, device=f"cuda:{comm.device}")
+
+
+def summarize_trace(buf: torch.Tensor, calls: int = 1) -> dict:
+    """Mean microseconds per CTA and call for every phase (the last entry is
+    table groups reduced per CTA and call)."""
+    m = buf.double().mean(dim=0).cpu() / max(calls, 1)
+    return {name: (round(float(v) / 1e3, 2) if name != "tgs_reduced" else round(float(v), 2))
+            for name, v in zip(TRACE_PHASES, m)}
+
+
 def stage_bytes_needed(n: int, dtype: torch.dtype, world: int, nblocks: int = 444, chunk_elems: int = 0) -> int:
     """Stage bytes of a native compressed allreduce of n elements; with
     ``chunk_elems`` > 0 the call runs in chunks of that many elements and
@@ -67,7 +96,7 @@ def stage_bytes_needed(n: int, dtype: torch.dtype, world: int, nblocks: int = 44
 def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=None,
                          nblocks: int = 0, multicast: bool = True, stream=None,
                          hybrid: bool = False, level="ans", chunk_bytes: int = 0,
-                         stage_local: bool = False) -> torch.Tensor:
+                         stage_local: bool = False, trace: torch.Tensor | None = None) -> torch.Tensor:
     """Sum-allreduce with lossless compression on the wire (native fused kernel).
 
     ``level``: codec level of the records, "ans" (rANS, best ratio) or "pack"
@@ -82,6 +111,9 @@ def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=
     ``stage_local`` encodes reduce-scatter records next to the encoding CTA
     and pushes them to the peer in 16-byte vectors instead of encoding
     straight into the peer's slot.
+    ``trace``: an int64 CUDA tensor from :func:`trace_buffer`; every CTA adds
+    the nanoseconds it spent in each phase (:data:`TRACE_PHASES`) to its row
+    (read with :func:`summarize_trace`).
 
     ``hybrid=True`` is the compressed P2P hybrid: the reduce-scatter moves raw
     bytes and only the all-gather of the reduced slices is compressed, so each
@@ -98,11 +130,15 @@ def compressed_allreduce(t: torch.Tensor, out: torch.Tensor | None = None, comm=
     s = stream or torch.cuda.current_stream(comm.device)
     nb = nblocks or comm.config.sm_budget
     chunk_elems = chunk_bytes // t.element_size() if chunk_bytes else 0
-    rc = comm._lib.lz_compressed_allreduce_chunked(comm.handle, t.data_ptr(), out.data_ptr(), t.numel(),
-                                                   lz_dtype(t.dtype), nb,
-                                                   int(multicast) | (2 if hybrid else 0) |
-                                                   (4 * codec.level_code(level)) | (8 if stage_local else 0),
-                                                   chunk_elems, s.cuda_stream)
+    if trace is not None and (trace.dtype != torch.int64 or not trace.is_cuda or
+                              trace.numel() < (nb or comm._lib.lz_cz_default_blocks(comm.handle)) * len(TRACE_PHASES)):
+        raise ValueError("trace must be the int64 CUDA tensor of trace_buffer(comm, nblocks)")
+    rc = comm._lib.lz_compressed_allreduce_traced(comm.handle, t.data_ptr(), out.data_ptr(), t.numel(),
+                                                  lz_dtype(t.dtype), nb,
+                                                  int(multicast) | (2 if hybrid else 0) |
+                                                  (4 * codec.level_code(level)) | (8 if stage_local else 0),
+                                                  chunk_elems, trace.data_ptr() if trace is not None else None,
+                                                  s.cuda_stream)
     _native.check(rc, "compressed_allreduce")
     return out
 

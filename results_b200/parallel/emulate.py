@@ -63,17 +63,19 @@ class EmulatedWorld:
         _native.check(rc, f"emulated allreduce[{algo}]")
 
     def compressed_allreduce(self, ins, outs, nblocks: int = 0, hybrid: bool = False, level="ans",
-                             chunk_elems: int = 0, stage_local: bool = False):
+                             chunk_elems: int = 0, stage_local: bool = False, trace=None):
+        """trace: int64 CUDA tensor [R, nblocks, phases] for the kernel's phase tracer."""
         from . import compressed  # noqa: F401  (declares the native signature)
         from ..ops import codec
 
         R = self.world
         arr_in = (C.c_void_p * R)(*[t.data_ptr() for t in ins])
         arr_out = (C.c_void_p * R)(*[t.data_ptr() for t in outs])
-        rc = self._lib.lz_emu_compressed_allreduce_chunked(self._emu, arr_in, arr_out, ins[0].numel(),
+        rc = self._lib.lz_emu_compressed_allreduce_traced(self._emu, arr_in, arr_out, ins[0].numel(),
                                                    lz_dtype(ins[0].dtype), nblocks,
                                                    (2 if hybrid else 0) | 4 * codec.level_code(level) |
                                                    (8 if stage_local else 0), chunk_elems,
+                                                   trace.data_ptr() if trace is not None else None,
                                                    torch.cuda.current_stream().cuda_stream)
         _native.check(rc, "emulated compressed allreduce")
 

@@ -127,3 +127,31 @@ def test_compressed_allreduce_stage_local(worlds, R, level, chunk):
     for r in range(R):
         assert w.status(r) == 0
         assert torch.equal(outs[r], ref), r
+
+
+@pytest.mark.parametrize("R", [2, 4])
+def test_compressed_allreduce_phase_tracer(worlds, R):
+    """The per-CTA phase tracer: every table group of every slice is reduced by
+    exactly one CTA, phase times are positive and their sum stays within the
+    CTA's total."""
+    from results_b200.parallel import compressed as cz
+
+    w = worlds[R]
+    G = 4
+    n = 32768 * R * 5 + 100
+    xs = _inputs(R, n, torch.bfloat16, seed=3)
+    outs = [torch.empty_like(x) for x in xs]
+    tr = torch.zeros((R, G, len(cz.TRACE_PHASES)), dtype=torch.int64, device="cuda")
+    w.compressed_allreduce(xs, outs, nblocks=G, level="pack", trace=tr)
+    torch.cuda.synchronize()
+    slice_elems = ((n + R - 1) // R + 15) // 16 * 16
+    tgs = [min(slice_elems, max(0, n - r * slice_elems)) for r in range(R)]
+    tgs = sum((t + 32767) // 32768 for t in tgs)
+    t = tr.cpu()
+    assert int(t[:, :, cz.TRACE_PHASES.index("tgs_reduced")].sum()) == tgs
+    total = t[:, :, 0]
+    parts = t[:, :, 1:cz.TRACE_PHASES.index("tgs_reduced")].sum(dim=2)
+    assert bool((total > 0).all()) and bool((parts <= total).all())
+    assert int(t[:, :, cz.TRACE_PHASES.index("rs_encode_push")].sum()) > 0
+    s = cz.summarize_trace(tr.view(R * G, -1))
+    assert s["total"] > 0 and set(s) == set(cz.TRACE_PHASES)
