@@ -178,3 +178,30 @@ def test_pack_invalid_code_in_partial_table_rejected():
 def test_unknown_level_rejected():
     with pytest.raises(ValueError):
         codec.encode_cpu(_rand(10, torch.bfloat16), level="zstd")
+
+
+def test_level_argument_encoding():
+    """Host entry points take the encoder level in bits 8..11 of the dtype argument."""
+    assert codec.level_code("ans") == 0 and codec.level_code("pack") == 1 and codec.level_code(1) == 1
+    assert codec.with_level(2, "pack") == 2 | (1 << 8) and codec.with_level(0, "ans") == 0
+    with pytest.raises(ValueError):
+        codec.level_code(7)
+
+
+def test_alltoall_compress_argument():
+    from results_b200.parallel.alltoall import enc_code
+
+    assert [enc_code(x) for x in (False, None, True, "ans", "pack")] == [0, 0, 1, 1, 2]
+    with pytest.raises(ValueError):
+        enc_code("zstd")
+
+
+def test_trace_summary_means_per_cta_and_call():
+    from results_b200.parallel import compressed as cz
+
+    buf = torch.zeros((4, len(cz.TRACE_PHASES)), dtype=torch.int64)
+    buf[:, 0] = 6000  # 6 us total per CTA over two calls
+    buf[:, cz.TRACE_PHASES.index("reduce")] = torch.tensor([1000, 2000, 3000, 4000])
+    buf[:, cz.TRACE_PHASES.index("tgs_reduced")] = 10
+    s = cz.summarize_trace(buf, calls=2)
+    assert s["total"] == 3.0 and s["reduce"] == 1.25 and s["tgs_reduced"] == 5.0
