@@ -1,7 +1,7 @@
 """Single-GPU timing of the multi-rank kernel bodies through the R-rank emulator.
 
     python -m results_b200.bench.emulated_bench --world 8 --mb 256 --algos oneshot,twoshot,compressed
-    (also: ll, a2a_raw, a2a_compressed, relay, wx_raw, wx_split)
+    (also: compressed_pack, hybrid_pack, ll, a2a_raw, a2a_compressed, relay, wx_raw, wx_split)
 
 Every emulated rank's heap lives on one GPU and the collective runs as one
 cooperative launch, so the numbers measure the kernel bodies (barriers,
@@ -72,6 +72,9 @@ def main(argv=None):
         check = True
         if algo == "compressed":
             fn = lambda: w.compressed_allreduce(ins, outs, nblocks=args.nblocks)  # noqa: E731
+        elif algo in ("compressed_pack", "hybrid_pack"):
+            fn = lambda h=(algo == "hybrid_pack"): w.compressed_allreduce(  # noqa: E731
+                ins, outs, nblocks=args.nblocks, hybrid=h, level="pack")
         elif algo in ("a2a_raw", "a2a_compressed"):
             fn = lambda c=(algo == "a2a_compressed"): w.all_to_all(ins, outs, compress=c,  # noqa: E731
                                                                    nblocks=args.nblocks)
