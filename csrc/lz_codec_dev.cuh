@@ -970,8 +970,16 @@ LZ_DEV bool rans_decode_sub(DecSmem& sm, const char* st, uint32_t len, uint32_t 
 // Decode the symbol plane of the TG record at `src` (n elements expected)
 // into sm.syms. Returns true on success (uniform over the CTA); the raw plane
 // starts at src + sizeof(TgHeader). A corrupt record returns false.
+// MODES: record modes compiled in (bit 1 << MODE_x); a record of another mode
+// is rejected as corrupt. Fused kernels that decode only their own level's
+// records drop the other decoder from their code.
 // ---------------------------------------------------------------------------
-template <int DT>
+constexpr int MODES_ALL = (1 << MODE_RAW) | (1 << MODE_ANS) | (1 << MODE_PACK);
+template <int LV>
+constexpr int kModesOfLevel =
+    LV == LEVEL_PACK ? ((1 << MODE_RAW) | (1 << MODE_PACK)) : ((1 << MODE_RAW) | (1 << MODE_ANS));
+
+template <int DT, int MODES = MODES_ALL>
 LZ_DEV bool decode_tg_syms(const char* __restrict__ src, uint32_t cap, uint32_t n, DecSmem& sm) {
   constexpr int RB = DT == DT_F32 ? 3 : (DT == DT_U8 ? 0 : 1);
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -984,11 +992,11 @@ LZ_DEV bool decode_tg_syms(const char* __restrict__ src, uint32_t cap, uint32_t 
              h.raw_bytes == pad16(n * RB) && h.total <= cap &&
              h.total == sizeof(TgHeader) + h.raw_bytes + h.sym_bytes;
     if (ok && h.mode == MODE_RAW) ok = h.sym_bytes == pad16(n);
-    else if (ok && h.mode == MODE_PACK)
+    else if (ok && ((MODES >> MODE_PACK) & 1) && h.mode == MODE_PACK)
       ok = h.nsub <= PACK_MAX_BITS && h.nnz >= 1 && h.reserved <= n &&
            (h.nsub == 0 ? (h.nnz == 1 && h.reserved == 0) : h.nnz <= (1u << h.nsub) - 1u) &&
            h.sym_bytes == pack_sym_bytes(n, h.nsub, h.reserved) && h.sym_bytes < pad16(n);
-    else if (ok && h.mode == MODE_ANS)
+    else if (ok && ((MODES >> MODE_ANS) & 1) && h.mode == MODE_ANS)
       ok = h.nsub == (n + SUB_ELEMS - 1) / SUB_ELEMS && h.nnz >= 1 && h.nnz <= 256 &&
            h.sym_bytes < pad16(n) &&
            pad16(4u * h.nnz) + pad16(4u * h.nsub) <= h.sym_bytes;
@@ -1004,8 +1012,10 @@ LZ_DEV bool decode_tg_syms(const char* __restrict__ src, uint32_t cap, uint32_t 
     for (uint32_t o = tid * 16; o < pad16(n); o += blockDim.x * 16)
       *reinterpret_cast<uint4*>(&sm.syms[o]) = ld_cg_v4(symsec + o);
   } else if (sm.h.mode == MODE_PACK) {
-    if (!pack_decode_syms(symsec, n, sm)) return false;
-  } else {
+    if constexpr (((MODES >> MODE_PACK) & 1) != 0) {
+      if (!pack_decode_syms(symsec, n, sm)) return false;
+    }
+  } else if constexpr (((MODES >> MODE_ANS) & 1) != 0) {
     const uint32_t nnz = sm.h.nnz, nsub = sm.h.nsub;
     // stage the whole ANS section (<= pad16(n) bytes) so every word fetch of
     // the rANS loop is a shared-memory load, off the global-latency path: one
@@ -1182,10 +1192,10 @@ LZ_DEV float elem_to_f32(uint8_t sym, const uint8_t* raw) {
 
 // Decode one TG record at `src` (n elements expected) into `out`.
 // Returns true on success (uniform over the CTA).
-template <int DT>
+template <int DT, int MODES = MODES_ALL>
 LZ_DEV bool decode_tg(const char* __restrict__ src, uint32_t cap, uint32_t n, char* __restrict__ out,
                       DecSmem& sm) {
-  if (!decode_tg_syms<DT>(src, cap, n, sm)) return false;
+  if (!decode_tg_syms<DT, MODES>(src, cap, n, sm)) return false;
   merge_store<DT>(src + sizeof(TgHeader), sm, n, out);
   return true;
 }

@@ -435,7 +435,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
             out_src = RedSrc{rec, nullptr};
             return true;
           }
-          if (!decode_tg_syms<DT>(rec, p.cap, tn, sm.dec)) {
+          if (!decode_tg_syms<DT, kModesOfLevel<LV>>(rec, p.cap, tn, sm.dec)) {
             if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 2, r);
             return false;
           }
@@ -496,7 +496,7 @@ __device__ __forceinline__ void cz_allreduce_body(const LzDevComm& c, const CzPa
       if (!wait_slot(ag_slot(c.heap[me], own, t, ck), 3, own)) return;
       lap(CZ_T_AG_WAIT);
       if (p.use_mc) fence_proxy_alias();  // the record arrived through the multicast mapping
-      if (!decode_tg<DT>(ag_slot(c.heap[me], own, t, ck), p.cap, tn, p.out + (s0 + (uint64_t)t * TG_ELEMS) * ES,
+      if (!decode_tg<DT, kModesOfLevel<LV>>(ag_slot(c.heap[me], own, t, ck), p.cap, tn, p.out + (s0 + (uint64_t)t * TG_ELEMS) * ES,
                          sm.dec)) {
         if (threadIdx.x == 0) lz_report(c, LZ_ERR_CORRUPT, 3, own);
         return;
