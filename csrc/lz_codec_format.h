@@ -36,9 +36,10 @@
 //            means every element's symbol is table[0].
 // The encoder has two levels. LEVEL_ANS codes a TG ANS only if no sub-stream
 // exceeds its sub-block's symbol count in bytes (before padding) and the ANS
-// section is smaller than the RAW section; otherwise RAW. LEVEL_PACK picks the
-// b in 0..4 with the smallest PACK section (ties: smaller b) and uses it when
-// it is smaller than the RAW section; otherwise RAW. PACK trades ratio (about
+// section is smaller than the RAW section; otherwise RAW. LEVEL_PACK picks,
+// among the b in 0..4 that escape at most n / 16 symbols, the one with the
+// smallest PACK section (ties: smaller b) and uses it when it is smaller than
+// the RAW section; otherwise RAW. PACK trades ratio (about
 // 3.3 code bits per bf16 exponent of N(0, s) data against ~2.7 for ANS) for
 // an encoder and decoder with a few integer operations per element. Decoding
 // accepts every mode and validates the magic, the sizes, that every word was
@@ -83,6 +84,7 @@ constexpr int CODEC_LEVEL_SHIFT = 8;
 constexpr uint32_t PACK_MAX_BITS = 4;
 constexpr uint32_t PACK_TABLE_BYTES = 16;
 constexpr uint32_t PACK_GROUP = 32;  // elements per code group
+constexpr uint32_t PACK_MAX_ESC_DIV = 16;  // at most n / 16 escaped symbols per table group
 
 // dtype codes (same values as LzDtype). The two fp8 "pair" types treat two
 // consecutive fp8 bytes as one 16-bit element: the pair is packed into a
@@ -149,6 +151,10 @@ LZC_HD PackChoice pack_choose(const uint32_t* top, uint32_t ntop, uint32_t n) {
     const uint32_t K = (1u << b) - 1u;
     for (; k < K && k < ntop; ++k) covered += top[k];
     const uint32_t nesc = n - covered;
+    // escapes are written one byte each: a width that escapes more than one
+    // symbol in 16 is not used (such groups are coded RAW), which keeps the
+    // level's cost per element bounded on data the table does not fit
+    if ((uint64_t)nesc * PACK_MAX_ESC_DIV > n) continue;
     const uint32_t bytes = pack_sym_bytes(n, b, nesc);
     if (bytes < best.bytes) best = PackChoice{(int)b, k, nesc, bytes};
   }
